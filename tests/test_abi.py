@@ -1,0 +1,103 @@
+"""The C-ABI library on a CPU-only machine: it loads, exports every symbol
+include/zengpu_b200.h declares, and its host-side logic answers without a
+GPU (no kernel is launched here)."""
+from __future__ import annotations
+
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+import zengpu_b200 as zg
+from zengpu_b200 import _lib as L
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "zengpu_b200.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(zg_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = zg.load_library()
+    names = declared_functions()
+    assert len(names) > 40
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    # the ctypes signature table covers the same set
+    assert set(L.SIGNATURES) == set(names)
+
+
+def test_abi_version():
+    assert zg.load_library().zg_abi_version() == 1
+
+
+@pytest.mark.parametrize("size,cls", [(0, 256), (1, 256), (255, 256), (256, 256), (257, 512),
+                                      (4097, 8192), (1 << 30, 1 << 30), ((1 << 30) + 1, 1 << 31)])
+def test_size_class(size, cls):
+    # zengpu-compute/src/pool.rs:91-104 plus the 1 GiB arrays of the bandwidth config
+    assert zg.size_class(size) == cls
+
+
+def test_no_device_is_reported_not_crashed():
+    if zg.device_count() > 0:
+        pytest.skip("a GPU is visible")
+    with pytest.raises(zg.NoDevice):
+        zg.CudaDevice(0)
+
+
+def test_workspace_bytes():
+    lib = zg.load_library()
+    assert lib.zg_sgemm_workspace_bytes(0, 1024, 1024, 1024) == 0
+    # TF32X3: hi/lo planes of A (m x k) and B (k x n), pitch rounded to 4
+    assert lib.zg_sgemm_workspace_bytes(1, 8192, 8192, 8192) == 4 * 8192 * 8192 * 4
+    assert lib.zg_sgemm_workspace_bytes(1, 17, 9, 33) == 2 * 256 * ((17 * 36 * 4 + 255) // 256) + \
+        2 * 256 * ((33 * 12 * 4 + 255) // 256)
+    # TF32: copies only when a pitch is not a multiple of 4 floats
+    assert lib.zg_sgemm_workspace_bytes(2, 64, 64, 64) == 0
+    assert lib.zg_sgemm_workspace_bytes(2, 17, 9, 33) > 0
+    assert lib.zg_sgemm_workspace_bytes(1, 0, 5, 5) == 0
+
+
+def test_sgemm_argument_errors_are_dispatch():
+    lib = zg.load_library()
+    fake = C.c_void_p(0x1000)
+    assert lib.zg_sgemm_f32(7, 4, 4, 4, 1.0, fake, fake, fake, None, 0, None, 0, None) == 11
+    assert "unknown mode" in L.last_error()
+    assert lib.zg_sgemm_f32(0, -1, 4, 4, 1.0, fake, fake, fake, None, 0, None, 0, None) == 11
+    assert lib.zg_sgemm_f32(0, 0, 4, 4, 1.0, None, None, None, None, 0, None, 0, None) == 0
+    assert lib.zg_sgemm_f32(0, 4, 4, 4, 1.0, None, fake, fake, None, 0, None, 0, None) == 11
+    # TF32X3 needs its hi/lo workspace
+    assert lib.zg_sgemm_f32(1, 64, 64, 64, 1.0, fake, fake, fake, None, 0, None, 0, None) == 11
+    assert "workspace" in L.last_error()
+
+
+def test_elementwise_argument_errors():
+    lib = zg.load_library()
+    assert lib.zg_add_f32(None, None, None, 0, None) == 0  # empty is a no-op
+    assert lib.zg_add_f32(None, None, None, 16, None) == 11
+    assert lib.zg_relu_f32(None, None, 16, None) == 11
+
+
+def test_error_classes_cover_every_status():
+    for code in range(1, 15):
+        assert code in zg.api._ERRORS
+    with pytest.raises(zg.Dispatch):
+        zg.api.check(11)
+    assert issubclass(zg.StaleHandle, zg.InvalidUsage)
+
+
+def test_dtype_sizes():
+    assert zg.DType.F32.size_bytes() == 4
+    assert zg.DType.F64.size_bytes() == 8
+    assert zg.DType.Bf16.size_bytes() == 2
+    assert zg.DType.Bool.size_bytes() == 1
+
+
+def test_product_path_does_not_reference_the_oracle():
+    pkg = Path(zg.__file__).resolve().parent
+    for p in list(pkg.rglob("*.py")) + list(pkg.rglob("*.cu")) + list(pkg.rglob("*.cpp")):
+        assert "oracle" not in p.read_text().lower(), p

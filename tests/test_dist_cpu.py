@@ -1,0 +1,82 @@
+"""Host logic of the M-row sharding on CPU: two gloo ranks, the per-shard
+compute stood in by a float64 CPU product (no GPU, no kernels here)."""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from zengpu_b200.dist import ShardedGemm, chunk_range, row_range
+
+
+@pytest.mark.parametrize("m,world", [(10, 3), (32768, 8), (7, 8), (0, 2), (8192, 1)])
+def test_row_range_partitions(m, world):
+    spans = [row_range(m, world, r) for r in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == m
+    for (a0, a1), (b0, b1) in zip(spans, spans[1:]):
+        assert a1 == b0
+    sizes = [b - a for a, b in spans]
+    assert max(sizes) - min(sizes) <= 1
+
+
+@pytest.mark.parametrize("n,world", [(1 << 28, 8), (1001, 3), (3, 4), (65536, 2)])
+def test_chunk_range_alignment(n, world):
+    spans = [chunk_range(n, world, r) for r in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == n
+    for (a0, a1), (b0, b1) in zip(spans, spans[1:]):
+        assert a1 == b0 and b0 % 4 == 0 or b0 == n
+
+
+def _cpu_compute(a, b, alpha, bias, relu, mode, out):
+    c = alpha * (a.double() @ b.double())
+    if bias is not None:
+        c = c + bias.double()
+    if relu:
+        c = torch.clamp_min(c, 0.0)
+    return c.float()
+
+
+def _worker(rank, world, port, m, n, k, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(0)
+        a = torch.rand((m, k), generator=g) * 2 - 1
+        b_full = torch.rand((k, n), generator=g) * 2 - 1
+        # only rank 0 holds the real B; the others must receive it
+        b = b_full.clone() if rank == 0 else torch.zeros_like(b_full)
+        sg = ShardedGemm(mode=1, compute=_cpu_compute)
+        r0, r1 = row_range(m, world, rank)
+        c_rows = sg.sgemm_rows(a[r0:r1].contiguous(), b, src=0, alpha=0.5)
+        c = sg.gather_rows(c_rows, m)
+        ref = 0.5 * (a.double() @ b_full.double())
+        q.put((rank, float((c.double() - ref).abs().max())))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_two_rank_broadcast_and_gather():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, 37, 19, 23, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, err in results:
+        assert err < 1e-5, (rank, err)

@@ -1,0 +1,166 @@
+"""f32 GEMM (SIMT, 3xTF32, TF32) and the fused bias+ReLU epilogue on the
+B200 against the oracle.  Tolerances (relative Frobenius error): SIMT and
+TF32X3 <= 1e-5, TF32 <= 5e-3; the integer KATs are exact in every mode."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import _oracle as O
+import zengpu_b200 as zg
+from zengpu_b200 import kernels as K
+
+pytestmark = pytest.mark.gpu
+
+MODES = [zg.GemmMode.SIMT_FP32, zg.GemmMode.TF32X3, zg.GemmMode.TF32]
+TOL = {zg.GemmMode.SIMT_FP32: 1e-5, zg.GemmMode.TF32X3: 1e-5, zg.GemmMode.TF32: 5e-3}
+
+
+def bits(x) -> np.ndarray:
+    return np.asarray(x, np.float32).view(np.uint32)
+
+
+def run(a: np.ndarray, b: np.ndarray, mode, alpha=1.0, bias=None, relu=False) -> np.ndarray:
+    ta, tb = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    tbias = torch.from_numpy(bias).cuda() if bias is not None else None
+    c = K.sgemm(ta, tb, mode=mode, alpha=alpha, bias=tbias, relu=relu)
+    torch.cuda.synchronize()
+    assert K.kernel_status() == 0
+    return c.cpu().numpy()
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_gemm_17x33x9_kat_exact(device, pool, kats, mode):
+    """zengpu-conformance/tests/devarray_matmul.rs:56-129 through GemmKernel."""
+    gemm = zg.GemmKernel(device, mode)
+    a = zg.upload(device, pool, kats["gemm_17x33x9_a"])
+    b = zg.upload(device, pool, kats["gemm_17x33x9_b"])
+    c = gemm.gemm(device, pool, a, b)
+    assert c.shape == [17, 9]
+    np.testing.assert_array_equal(bits(zg.download(device, c)), bits(kats["gemm_17x33x9_c"]))
+    gemm.destroy(device)
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_op_graph_chain(device, pool, kats, mode):
+    """examples/op_graph_lower.rs: Matmul -> Add -> Relu as three dispatches."""
+    gemm = zg.GemmKernel(device, mode)
+    ew = zg.ElementwiseKernels(device)
+    a = zg.upload(device, pool, kats["op_graph_8x4x6_a"])
+    b = zg.upload(device, pool, kats["op_graph_8x4x6_b"])
+    c = zg.upload(device, pool, kats["op_graph_8x4x6_c"])
+    y = ew.relu(device, pool, ew.add(device, pool, gemm.gemm(device, pool, a, b), c))
+    np.testing.assert_array_equal(bits(zg.download(device, y)), bits(kats["op_graph_8x4x6_y"]))
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_tiled_and_heavy_patterns(kats, mode):
+    c = run(kats["tiled_31x29x23_a"], kats["tiled_31x29x23_b"], mode)
+    assert np.max(np.abs(c - kats["tiled_31x29x23_c64"])) < 1e-3
+    h = run(kats["heavy_64x48x40_a"], kats["heavy_64x48x40_b"], mode)
+    ref = kats["heavy_64x48x40_c64"]
+    assert np.all(np.abs(h - ref) / np.maximum(np.abs(ref), 1.0) <= 0.01)
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_config0_256_parity(mode):
+    """M=N=K=256, A,B uniform[-1,1) seed 0 (one stream, A then B)."""
+    ab = O.uniform(2 * 256 * 256, 0)
+    a, b = ab[: 256 * 256].reshape(256, 256), ab[256 * 256:].reshape(256, 256)
+    c = run(a, b, mode)
+    assert O.rel_fro(c, O.sgemm_ref(a, b)) <= TOL[mode]
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_1024_parity_vs_oracle(mode):
+    a = O.uniform(1024 * 1024, 2).reshape(1024, 1024)
+    b = O.uniform(1024 * 1024, 102).reshape(1024, 1024)
+    c = run(a, b, mode)
+    ref = O.sgemm(a, b)
+    err = O.rel_fro(c, ref)
+    assert err <= TOL[mode], err
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("size", [2048, 4096])
+def test_large_sampled_vs_fp64(mode, size):
+    ta = torch.empty((size, size), device="cuda")
+    tb = torch.empty((size, size), device="cuda")
+    K.fill_uniform(ta, 2)
+    K.fill_uniform(tb, 3)
+    c = K.sgemm(ta, tb, mode=mode)
+    torch.cuda.synchronize()
+    assert K.kernel_status() == 0
+    a, b = ta.cpu().numpy(), tb.cpu().numpy()
+    for r0, c0 in [(0, 0), (size - 256, size - 256), (size // 2 - 100, 37)]:
+        ref = O.dgemm_tile(a, b, r0, c0, 256, 256)
+        got = c[r0:r0 + 256, c0:c0 + 256].cpu().numpy()
+        assert O.rel_fro(got, ref) <= TOL[mode]
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (3, 5, 7), (129, 257, 33), (200, 300, 130),
+                                   (130, 70, 1000), (257, 513, 31), (64, 8, 4096)])
+def test_odd_shapes(mode, m, n, k):
+    a = O.uniform(m * k, 21).reshape(m, k)
+    b = O.uniform(k * n, 22).reshape(k, n)
+    for alpha in (1.0, -0.5):
+        c = run(a, b, mode, alpha=alpha)
+        assert O.rel_fro(c, O.sgemm(a, b, alpha)) <= max(TOL[mode], 2e-6)
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_k_zero(mode):
+    a = np.zeros((5, 0), np.float32)
+    b = np.zeros((0, 7), np.float32)
+    c = run(a, b, mode, alpha=-1.0)
+    np.testing.assert_array_equal(bits(c), bits(O.sgemm_ref(a, b, -1.0)))
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("m,n,k", [(256, 256, 256), (300, 520, 72)])
+def test_fused_bias_relu(mode, m, n, k):
+    a = O.normal(m * k, 3).reshape(m, k)
+    b = O.uniform(k * n, 4, -0.038, 0.038).reshape(k, n)
+    bias = O.uniform(n, 5, -0.1, 0.1)
+    y = run(a, b, mode, alpha=1.0, bias=bias, relu=True)
+    ref = O.sgemm_bias_relu(a, b, bias)
+    assert O.rel_fro(y, ref) <= TOL[mode]
+    assert (y >= 0).all() and not np.signbit(y).any()
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_fused_api_matches_unfused_chain(device, pool, mode):
+    m, n, k = 96, 160, 48
+    a = O.normal(m * k, 8).reshape(m, k)
+    b = O.uniform(k * n, 9).reshape(k, n)
+    bias = O.uniform(n, 10, -0.1, 0.1)
+    gemm = zg.GemmKernel(device, mode)
+    ew = zg.ElementwiseKernels(device)
+    da, db, dbias = (zg.upload(device, pool, x) for x in (a, b, bias))
+    fused = zg.download(device, gemm.gemm_bias_relu(device, pool, 1.0, da, db, dbias))
+    dbias_full = zg.upload(device, pool, np.broadcast_to(bias, (m, n)))
+    unfused = ew.relu(device, pool, ew.add(device, pool, gemm.gemm(device, pool, da, db), dbias_full))
+    np.testing.assert_array_equal(bits(fused), bits(zg.download(device, unfused)))
+
+
+def test_gemm_api_errors(device, pool):
+    gemm = zg.GemmKernel(device)
+    a = pool.alloc([4, 8], zg.DType.F32)
+    b = pool.alloc([7, 3], zg.DType.F32)
+    v = pool.alloc([8], zg.DType.F32)
+    i = pool.alloc([8, 3], zg.DType.I32)
+    with pytest.raises(zg.Dispatch, match="inner dimensions mismatch"):
+        gemm.gemm(device, pool, a, b)
+    with pytest.raises(zg.Dispatch, match="expected 2D"):
+        gemm.gemm(device, pool, a, v)
+    with pytest.raises(zg.Dispatch, match="only f32"):
+        gemm.gemm(device, pool, a, i)
+    good_b = pool.alloc([8, 3], zg.DType.F32)
+    with pytest.raises(zg.Dispatch, match="bias shape"):
+        gemm.gemm_bias_relu(device, pool, 1.0, a, good_b, v)
+
+
+def test_default_mode_is_tf32x3(device):
+    assert zg.GemmKernel(device).mode == zg.GemmMode.TF32X3

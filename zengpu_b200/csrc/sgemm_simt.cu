@@ -1,0 +1,168 @@
+// sgemm_simt.cu - exact-fp32 CUDA-core SGEMM, the accuracy anchor of the GEMM
+// family.  Replaces the one-thread-per-element GEMM_PTX / GEMM_ZSL kernels
+// (zengpu-blas/src/level3.rs:13-90): same contract, C = alpha * A @ B with
+// row-major f32 operands, plus the optional fused bias/ReLU epilogue.
+//
+// Design: 128x128 CTA tile, BK = 16, 256 threads, each thread an 8x8 register
+// tile laid out as 2x2 blocks of 4x4 so every shared-memory read is a
+// conflict-free 128-bit load.  A is stored transposed (k-major) in shared
+// memory; tiles are double buffered with register staging: the global loads
+// for tile t+1 are in flight while tile t is multiplied.  Products are
+// accumulated with fmaf (IEEE fma, as GEMM_PTX's fma.rn.f32).
+#include <cstdint>
+
+#include "zg_common.cuh"
+
+namespace zg {
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 16;
+constexpr int kThreads = 256;
+constexpr int kPadA = 4;  // As row pitch 132 floats: 16-byte aligned rows
+
+template <bool kVecA, bool kVecB>
+__global__ void __launch_bounds__(kThreads, 2)
+    sgemm_simt_kernel(int M, int N, int K, float alpha, const float* __restrict__ A,
+                      const float* __restrict__ B, float* __restrict__ C,
+                      const float* __restrict__ bias, int relu, int vec_c) {
+    __shared__ __align__(16) float As[2][BK][BM + kPadA];
+    __shared__ __align__(16) float Bs[2][BK][BN];
+
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+
+    // Global-load mapping.  A: 2 x (row, 4 k) per thread.  B: 2 x (k, 4 n).
+    const int a_row = tid >> 2, a_kq = (tid & 3) * 4;
+    const int b_k = tid >> 5, b_nq = (tid & 31) * 4;
+
+    float4 ra[2], rb[2];
+
+    auto load_tile = [&](int k0) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int row = m0 + a_row + 64 * j;
+            const int kk = k0 + a_kq;
+            if (kVecA) {
+                ra[j] = (row < M && kk < K)
+                            ? __ldg(reinterpret_cast<const float4*>(A + (size_t)row * K + kk))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            } else {
+                float v[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    v[c] = (row < M && kk + c < K) ? __ldg(A + (size_t)row * K + kk + c) : 0.f;
+                ra[j] = make_float4(v[0], v[1], v[2], v[3]);
+            }
+            const int krow = k0 + b_k + 8 * j;
+            const int col = n0 + b_nq;
+            if (kVecB) {
+                rb[j] = (krow < K && col < N)
+                            ? __ldg(reinterpret_cast<const float4*>(B + (size_t)krow * N + col))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            } else {
+                float v[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    v[c] = (krow < K && col + c < N) ? __ldg(B + (size_t)krow * N + col + c) : 0.f;
+                rb[j] = make_float4(v[0], v[1], v[2], v[3]);
+            }
+        }
+    };
+    auto store_tile = [&](int buf) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int row = a_row + 64 * j;
+            As[buf][a_kq + 0][row] = ra[j].x;
+            As[buf][a_kq + 1][row] = ra[j].y;
+            As[buf][a_kq + 2][row] = ra[j].z;
+            As[buf][a_kq + 3][row] = ra[j].w;
+            *reinterpret_cast<float4*>(&Bs[buf][b_k + 8 * j][b_nq]) = rb[j];
+        }
+    };
+
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+    const int nk = (K + BK - 1) / BK;
+    if (nk > 0) {
+        load_tile(0);
+        store_tile(0);
+    }
+    __syncthreads();
+    for (int kt = 0; kt < nk; ++kt) {
+        const int buf = kt & 1;
+        if (kt + 1 < nk) load_tile((kt + 1) * BK);
+#pragma unroll
+        for (int k = 0; k < BK; ++k) {
+            const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][k][64 + ty * 4]);
+            const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 4]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][k][64 + tx * 4]);
+            const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        if (kt + 1 < nk) store_tile(buf ^ 1);
+        __syncthreads();
+    }
+
+    // Epilogue: c = alpha*acc, then + bias[col], then ReLU, each rounded.
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+        if (row >= M) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int col = n0 + h * 64 + tx * 4;
+            float v[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float x = __fmul_rn(alpha, acc[i][h * 4 + c]);
+                if (bias && col + c < N) x = __fadd_rn(x, __ldg(bias + col + c));
+                if (relu) x = relu1(x);
+                v[c] = x;
+            }
+            float* dst = C + (size_t)row * N + col;
+            if (vec_c && col + 3 < N) {
+                *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    if (col + c < N) dst[c] = v[c];
+            }
+        }
+    }
+}
+
+}  // namespace
+
+// Launches the SIMT SGEMM on `stream`; shapes already validated by the caller.
+int launch_sgemm_simt(int M, int N, int K, float alpha, const float* A, const float* B, float* C,
+                      const float* bias, int relu, cudaStream_t stream) {
+    const bool va = (K % 4 == 0) && ((reinterpret_cast<uintptr_t>(A) & 15u) == 0);
+    const bool vb = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(B) & 15u) == 0);
+    const int vc = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
+    dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+    if (va && vb)
+        sgemm_simt_kernel<true, true><<<grid, kThreads, 0, stream>>>(M, N, K, alpha, A, B, C, bias,
+                                                                     relu, vc);
+    else if (va)
+        sgemm_simt_kernel<true, false><<<grid, kThreads, 0, stream>>>(M, N, K, alpha, A, B, C,
+                                                                      bias, relu, vc);
+    else if (vb)
+        sgemm_simt_kernel<false, true><<<grid, kThreads, 0, stream>>>(M, N, K, alpha, A, B, C,
+                                                                      bias, relu, vc);
+    else
+        sgemm_simt_kernel<false, false><<<grid, kThreads, 0, stream>>>(M, N, K, alpha, A, B, C,
+                                                                       bias, relu, vc);
+    return cuda_status(cudaGetLastError(), "sgemm_simt");
+}
+
+}  // namespace zg

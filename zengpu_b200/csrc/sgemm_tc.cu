@@ -1,0 +1,516 @@
+// sgemm_tc.cu - tcgen05 / TMEM tensor-core SGEMM for sm_100a, and the GEMM
+// dispatcher behind zg_sgemm_f32 (the kernel contract of GEMM_PTX's entry
+// `main(a, b, c, m, n, k, alpha)`, zengpu-blas/src/level3.rs:35-90).
+//
+// Two tensor-core modes share one kernel template:
+//   TF32    one kind::tf32 MMA per k-step on the raw f32 operands;
+//   TF32X3  split precision: x = hi + lo with hi = tf32(x), lo = tf32(x - hi)
+//           (round-to-nearest both), D += A_lo*B_hi + A_hi*B_lo + A_hi*B_hi;
+//           the dropped lo*lo term is ~2^-22 relative, so the result keeps
+//           fp32-class accuracy.  A pre-pass writes the hi/lo planes.
+//
+// Kernel layout (one 128 x 256 output tile per CTA, 192 threads):
+//   warp 0      TMA producer: A tile [128 x BK] K-major and B tile [BK x 256]
+//               N-major (B stays row-major in HBM; the MMA reads it MN-major),
+//               128-byte swizzled, into a STAGES-deep mbarrier ring;
+//   warp 1      allocates 256 TMEM columns (the f32 accumulator, lane = row)
+//               and one thread issues tcgen05.mma, committing each stage back
+//               to the producer and the finished tile to the epilogue;
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, alpha / bias /
+//               ReLU in registers, 128-bit stores.
+// Every mbarrier wait is bounded (zg_common.cuh); an expiry sets a bit in the
+// device status word, the kernel drains its in-flight copies and MMAs, frees
+// TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "zg_common.cuh"
+
+namespace zg {
+
+__device__ uint32_t g_status = 0;
+
+int launch_sgemm_simt(int M, int N, int K, float alpha, const float* A, const float* B, float* C,
+                      const float* bias, int relu, cudaStream_t stream);
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int kChunk = 32;  // f32 columns per 128-byte swizzle row
+constexpr int kTcThreads = 192;
+constexpr uint32_t kTmemCols = 256;
+
+template <int kPlanes>
+struct TcCfg {
+    static constexpr int BK = kPlanes == 1 ? 32 : 16;      // k per stage
+    static constexpr int STAGES = 4;                       // 48 KB per stage
+    static constexpr int A_BYTES = BM * BK * 4;            // one plane
+    static constexpr int B_CHUNK_BYTES = BK * kChunk * 4;  // one 32-col chunk
+    static constexpr int B_BYTES = BN * BK * 4;            // one plane
+    static constexpr int STAGE_BYTES = kPlanes * (A_BYTES + B_BYTES);
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*bars*/;
+    // A descriptor: K-major, swizzle width = BK*4 bytes (128B or 64B).
+    static constexpr uint32_t A_LAYOUT = BK == 32 ? 2u : 4u;  // SWIZZLE_128B : SWIZZLE_64B
+    static constexpr uint32_t A_SBO = 8 * BK * 4;             // 8-row core-matrix group
+};
+
+struct TcMaps {
+    CUtensorMap a[2];  // hi, lo (TF32 uses a[0] only)
+    CUtensorMap b[2];
+};
+
+// UMMA shared-memory descriptor (sm100): start, leading / stride byte
+// offsets (16-byte units), version 1, layout type in bits 61-63.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) |
+           (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) |
+           (static_cast<uint64_t>(layout) << 61);
+}
+
+// Instruction descriptor, kind::tf32: D f32, A/B tf32, A K-major, B MN-major,
+// M = 128, N = 256.
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (0u << 15) | (1u << 16) |
+                            (static_cast<uint32_t>(BN >> 3) << 17) |
+                            (static_cast<uint32_t>(BM >> 4) << 24);
+
+// Grouped raster: consecutive CTAs walk down kGroupM row-tiles before moving
+// right, so CTAs resident together share A row-blocks and B column-blocks in L2.
+constexpr int kGroupM = 16;
+__device__ __forceinline__ void tile_coords(int tile, int mt, int nt, int& m_tile, int& n_tile) {
+    const int group_size = kGroupM * nt;
+    const int group = tile / group_size;
+    const int first_m = group * kGroupM;
+    const int gm = min(mt - first_m, kGroupM);
+    const int r = tile - group * group_size;
+    m_tile = first_m + r % gm;
+    n_tile = r / gm;
+}
+
+template <int kPlanes>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    sgemm_tc_kernel(const __grid_constant__ TcMaps maps, int M, int N, int K, float alpha,
+                    float* __restrict__ C, const float* __restrict__ bias, int relu, int vec_c) {
+    using Cfg = TcCfg<kPlanes>;
+    constexpr int BK = Cfg::BK, STAGES = Cfg::STAGES;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* accum_full = empty + STAGES;
+    uint64_t* drain = accum_full + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
+    int m_tile, n_tile;
+    tile_coords(blockIdx.x, mt, nt, m_tile, n_tile);
+    const int m0 = m_tile * BM, n0 = n_tile * BN;
+    const int nkb = (K + BK - 1) / BK;
+
+    auto a_plane = [&](int s, int p) { return smem + s * Cfg::STAGE_BYTES + p * Cfg::A_BYTES; };
+    auto b_plane = [&](int s, int p) {
+        return smem + s * Cfg::STAGE_BYTES + kPlanes * Cfg::A_BYTES + p * Cfg::B_BYTES;
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum_full, 1);
+        mbar_init(drain, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        for (int p = 0; p < kPlanes; ++p) {
+            prefetch_tensormap(&maps.a[p]);
+            prefetch_tensormap(&maps.b[p]);
+        }
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int issued = 0;
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t ph = (kb / STAGES) & 1;
+                if (!mbar_wait_bounded(&empty[s], ph ^ 1, &g_status, kErrTcProducer)) break;
+                mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+                const int k0 = kb * BK;
+                for (int p = 0; p < kPlanes; ++p) {
+                    tma_load_2d(a_plane(s, p), &maps.a[p], k0, m0, &full[s]);
+                    uint8_t* bp = b_plane(s, p);
+#pragma unroll
+                    for (int c = 0; c < BN / kChunk; ++c)
+                        tma_load_2d(bp + c * Cfg::B_CHUNK_BYTES, &maps.b[p], n0 + c * kChunk, k0,
+                                    &full[s]);
+                }
+                issued = kb + 1;
+            }
+            // Make sure no copy is still landing in shared memory at exit.
+            const int first = issued > STAGES ? issued - STAGES : 0;
+            for (int kb = first; kb < issued; ++kb)
+                mbar_wait_bounded(&full[kb % STAGES], (kb / STAGES) & 1, &g_status, kErrTcDrain);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            bool ok = true;
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t ph = (kb / STAGES) & 1;
+                if (!mbar_wait_bounded(&full[s], ph, &g_status, kErrTcMma)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(a_plane(s, 0));
+                const uint32_t b0 = smem_u32(b_plane(s, 0));
+#pragma unroll
+                for (int kk = 0; kk < BK / 8; ++kk) {
+                    // A: advance 8 f32 (32 bytes) inside the swizzle row.
+                    // B: advance one 8-row (1024-byte) core-matrix group.
+                    const uint64_t ahi = umma_desc(a0 + kk * 32, 16, Cfg::A_SBO, Cfg::A_LAYOUT);
+                    const uint64_t bhi =
+                        umma_desc(b0 + kk * 1024, Cfg::B_CHUNK_BYTES, 1024, 2u);
+                    const uint32_t acc0 = (kb | kk) != 0;
+                    if (kPlanes == 2) {
+                        const uint32_t a1 = smem_u32(a_plane(s, 1));
+                        const uint32_t b1 = smem_u32(b_plane(s, 1));
+                        const uint64_t alo =
+                            umma_desc(a1 + kk * 32, 16, Cfg::A_SBO, Cfg::A_LAYOUT);
+                        const uint64_t blo =
+                            umma_desc(b1 + kk * 1024, Cfg::B_CHUNK_BYTES, 1024, 2u);
+                        mma_tf32_ss(tmem_base, alo, bhi, kIdesc, acc0);
+                        mma_tf32_ss(tmem_base, ahi, blo, kIdesc, 1u);
+                        mma_tf32_ss(tmem_base, ahi, bhi, kIdesc, 1u);
+                    } else {
+                        mma_tf32_ss(tmem_base, ahi, bhi, kIdesc, acc0);
+                    }
+                }
+                mma_commit(&empty[s]);  // stage s free once these MMAs finish
+            }
+            if (ok) {
+                mma_commit(accum_full);
+            } else {
+                mma_commit(drain);
+                mbar_wait_bounded(drain, 0, &g_status, kErrTcDrain);
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int row = m0 + q * 32 + lane;
+        const bool ok = mbar_wait_bounded(accum_full, 0, &g_status, kErrTcEpilogue);
+        tc_fence_after();
+        if (ok) {
+#pragma unroll 1
+            for (int cc = 0; cc < BN / 32; ++cc) {
+                const int col0 = n0 + cc * 32;
+                if (col0 >= N) break;
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + cc * 32, r);
+                if (row < M) {
+                    float v[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        float x = __fmul_rn(alpha, __uint_as_float(r[j]));
+                        if (bias) x = __fadd_rn(x, col0 + j < N ? __ldg(bias + col0 + j) : 0.0f);
+                        if (relu) x = relu1(x);
+                        v[j] = x;
+                    }
+                    float* dst = C + static_cast<size_t>(row) * N + col0;
+                    if (vec_c && col0 + 32 <= N) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4*>(dst + j) =
+                                make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < N) dst[j] = v[j];
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ---- split / pad pre-pass ---------------------------------------------------
+// dst_hi[r, c] = tf32(src[r, c]); dst_lo[r, c] = tf32(src - hi) (when non-null);
+// rows of `cols` elements, source pitch `lds`, destination pitch `ldd`.
+// With dst_lo == null and round == 0 it is a plain pitched copy.
+__global__ void __launch_bounds__(256)
+    split_planes_kernel(const float* __restrict__ src, int rows, int cols, int64_t lds,
+                        float* __restrict__ hi, float* __restrict__ lo, int64_t ldd, int round) {
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+        const float* s = src + r * lds;
+        float* h = hi + r * ldd;
+        float* l = lo ? lo + r * ldd : nullptr;
+        for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+            const float x = __ldcs(s + c);
+            const float xh = round ? to_tf32(x) : x;
+            h[c] = xh;
+            if (l) l[c] = to_tf32(__fsub_rn(x, xh));
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256)
+    split_planes_vec_kernel(const float4* __restrict__ src, int rows, int cols4, int64_t lds4,
+                            float4* __restrict__ hi, float4* __restrict__ lo, int64_t ldd4) {
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+        const float4* s = src + r * lds4;
+        float4* h = hi + r * ldd4;
+        float4* l = lo + r * ldd4;
+        for (int c = threadIdx.x; c < cols4; c += blockDim.x) {
+            const float4 x = __ldcs(s + c);
+            const float4 xh = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
+            h[c] = xh;
+            l[c] = make_float4(to_tf32(__fsub_rn(x.x, xh.x)), to_tf32(__fsub_rn(x.y, xh.y)),
+                               to_tf32(__fsub_rn(x.z, xh.z)), to_tf32(__fsub_rn(x.w, xh.w)));
+        }
+    }
+}
+
+// C = epilogue(alpha * 0) for K == 0 (an empty sum, as the reference loop).
+__global__ void gemm_k0_kernel(int M, int N, float alpha, float* C, const float* bias, int relu) {
+    const int64_t total = static_cast<int64_t>(M) * N;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float x = __fmul_rn(alpha, 0.0f);
+        if (bias) x = __fadd_rn(x, bias[i % N]);
+        if (relu) x = relu1(x);
+        C[i] = x;
+    }
+}
+
+// ---- host side ----------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
+                                             cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D row-major f32 map: inner extent `cols`, outer `rows`, pitch `ld`
+// elements, box {box_x, box_y}.
+int encode_map(CUtensorMap* map, const float* base, uint64_t cols, uint64_t rows, uint64_t ld,
+               uint32_t box_x, uint32_t box_y, CUtensorMapSwizzle swz) {
+    auto fn = get_encode_fn();
+    if (!fn) return set_error(ZG_ERR_BACKEND, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld * 4};
+    cuuint32_t box[2] = {box_x, box_y};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(ZG_ERR_BACKEND, "cuTensorMapEncodeTiled failed (%d): %llux%llu ld=%llu",
+                         static_cast<int>(r), (unsigned long long)rows, (unsigned long long)cols,
+                         (unsigned long long)ld);
+    return ZG_OK;
+}
+
+uint64_t round_up(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct WsLayout {
+    uint64_t a_hi, a_lo, b_hi, b_lo, total;  // byte offsets; ~0 = unused
+};
+
+constexpr uint64_t kNone = ~0ull;
+
+WsLayout ws_layout(int mode, int m, int n, int k) {
+    WsLayout w{kNone, kNone, kNone, kNone, 0};
+    const uint64_t kp = round_up(k, 4), np = round_up(n, 4);
+    const uint64_t a_bytes = round_up(static_cast<uint64_t>(m) * kp * 4, 256);
+    const uint64_t b_bytes = round_up(static_cast<uint64_t>(k) * np * 4, 256);
+    uint64_t off = 0;
+    if (mode == ZG_GEMM_TF32X3) {
+        w.a_hi = off; off += a_bytes;
+        w.a_lo = off; off += a_bytes;
+        w.b_hi = off; off += b_bytes;
+        w.b_lo = off; off += b_bytes;
+    } else if (mode == ZG_GEMM_TF32) {
+        if (k % 4 != 0) { w.a_hi = off; off += a_bytes; }
+        if (n % 4 != 0) { w.b_hi = off; off += b_bytes; }
+    }
+    w.total = off;
+    return w;
+}
+
+unsigned split_grid(int rows) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int cap = sms * 8;
+    return static_cast<unsigned>(rows < cap ? (rows < 1 ? 1 : rows) : cap);
+}
+
+// Writes the tf32 hi (and lo) planes of a rows x cols matrix into pitch-ldd
+// buffers; a plain pitched copy when lo == null and round == 0.
+int launch_split(const float* src, int rows, int cols, int64_t lds, float* hi, float* lo,
+                 int64_t ldd, int round, cudaStream_t s) {
+    if (rows == 0 || cols == 0) return ZG_OK;
+    if (lo && round && cols % 4 == 0 && lds % 4 == 0 && ldd % 4 == 0 && aligned16(src) &&
+        aligned16(hi) && aligned16(lo)) {
+        split_planes_vec_kernel<<<split_grid(rows), 256, 0, s>>>(
+            reinterpret_cast<const float4*>(src), rows, cols / 4, lds / 4,
+            reinterpret_cast<float4*>(hi), reinterpret_cast<float4*>(lo), ldd / 4);
+    } else {
+        split_planes_kernel<<<split_grid(rows), 256, 0, s>>>(src, rows, cols, lds, hi, lo, ldd,
+                                                             round);
+    }
+    return cuda_status(cudaGetLastError(), "sgemm split pre-pass");
+}
+
+template <int kPlanes>
+int launch_tc(const TcMaps& maps, int M, int N, int K, float alpha, float* C, const float* bias,
+              int relu, cudaStream_t s) {
+    using Cfg = TcCfg<kPlanes>;
+    static std::once_flag attr_once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(attr_once, [] {
+        attr_err = cudaFuncSetAttribute(sgemm_tc_kernel<kPlanes>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        Cfg::SMEM_BYTES);
+    });
+    if (attr_err != cudaSuccess) return cuda_status(attr_err, "sgemm_tc smem attribute");
+    const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
+    const int vec_c = (N % 4 == 0) && aligned16(C);
+    sgemm_tc_kernel<kPlanes><<<mt * nt, kTcThreads, Cfg::SMEM_BYTES, s>>>(maps, M, N, K, alpha, C,
+                                                                         bias, relu, vec_c);
+    return cuda_status(cudaGetLastError(), "sgemm_tc");
+}
+
+int sgemm_tensor_core(int mode, int M, int N, int K, float alpha, const float* A, const float* B,
+                      float* C, const float* bias, int relu, uint8_t* ws, cudaStream_t s) {
+    const WsLayout w = ws_layout(mode, M, N, K);
+    const int64_t kp = static_cast<int64_t>(round_up(K, 4));
+    const int64_t np = static_cast<int64_t>(round_up(N, 4));
+    TcMaps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    int rc;
+    if (mode == ZG_GEMM_TF32X3) {
+        float* ahi = reinterpret_cast<float*>(ws + w.a_hi);
+        float* alo = reinterpret_cast<float*>(ws + w.a_lo);
+        float* bhi = reinterpret_cast<float*>(ws + w.b_hi);
+        float* blo = reinterpret_cast<float*>(ws + w.b_lo);
+        if ((rc = launch_split(A, M, K, K, ahi, alo, kp, 1, s)) != ZG_OK) return rc;
+        if ((rc = launch_split(B, K, N, N, bhi, blo, np, 1, s)) != ZG_OK) return rc;
+        const CUtensorMapSwizzle aswz = TcCfg<2>::BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                                            : CU_TENSOR_MAP_SWIZZLE_64B;
+        if ((rc = encode_map(&maps.a[0], ahi, K, M, kp, TcCfg<2>::BK, BM, aswz)) != ZG_OK) return rc;
+        if ((rc = encode_map(&maps.a[1], alo, K, M, kp, TcCfg<2>::BK, BM, aswz)) != ZG_OK) return rc;
+        if ((rc = encode_map(&maps.b[0], bhi, N, K, np, kChunk, TcCfg<2>::BK,
+                             CU_TENSOR_MAP_SWIZZLE_128B)) != ZG_OK)
+            return rc;
+        if ((rc = encode_map(&maps.b[1], blo, N, K, np, kChunk, TcCfg<2>::BK,
+                             CU_TENSOR_MAP_SWIZZLE_128B)) != ZG_OK)
+            return rc;
+        return launch_tc<2>(maps, M, N, K, alpha, C, bias, relu, s);
+    }
+    // TF32: raw operands, or pitch-padded copies when a pitch is not 16-byte aligned.
+    const float* a_src = A;
+    int64_t lda = K;
+    if (w.a_hi != kNone) {
+        float* ap = reinterpret_cast<float*>(ws + w.a_hi);
+        if ((rc = launch_split(A, M, K, K, ap, nullptr, kp, 0, s)) != ZG_OK) return rc;
+        a_src = ap;
+        lda = kp;
+    }
+    const float* b_src = B;
+    int64_t ldb = N;
+    if (w.b_hi != kNone) {
+        float* bp = reinterpret_cast<float*>(ws + w.b_hi);
+        if ((rc = launch_split(B, K, N, N, bp, nullptr, np, 0, s)) != ZG_OK) return rc;
+        b_src = bp;
+        ldb = np;
+    }
+    if (!aligned16(a_src) || !aligned16(b_src))
+        return set_error(ZG_ERR_DISPATCH,
+                         "sgemm (TF32 mode): A and B must start on a 16-byte boundary");
+    if ((rc = encode_map(&maps.a[0], a_src, K, M, lda, TcCfg<1>::BK, BM,
+                         CU_TENSOR_MAP_SWIZZLE_128B)) != ZG_OK)
+        return rc;
+    if ((rc = encode_map(&maps.b[0], b_src, N, K, ldb, kChunk, TcCfg<1>::BK,
+                         CU_TENSOR_MAP_SWIZZLE_128B)) != ZG_OK)
+        return rc;
+    return launch_tc<1>(maps, M, N, K, alpha, C, bias, relu, s);
+}
+
+}  // namespace
+}  // namespace zg
+
+using namespace zg;
+
+extern "C" uint64_t zg_sgemm_workspace_bytes(int mode, int m, int n, int k) {
+    if (m <= 0 || n <= 0 || k <= 0) return 0;
+    return ws_layout(mode, m, n, k).total;
+}
+
+extern "C" int zg_sgemm_f32(int mode, int m, int n, int k, float alpha, const float* a,
+                            const float* b, float* c, const float* bias, int relu,
+                            void* workspace, uint64_t workspace_bytes, void* stream) {
+    if (mode != ZG_GEMM_SIMT_FP32 && mode != ZG_GEMM_TF32X3 && mode != ZG_GEMM_TF32)
+        return set_error(ZG_ERR_DISPATCH, "sgemm: unknown mode %d", mode);
+    if (m < 0 || n < 0 || k < 0)
+        return set_error(ZG_ERR_DISPATCH, "sgemm: negative shape %d x %d x %d", m, n, k);
+    if (m == 0 || n == 0) return ZG_OK;
+    if (!c || (k > 0 && (!a || !b)))
+        return set_error(ZG_ERR_DISPATCH, "sgemm: null operand pointer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (k == 0) {
+        gemm_k0_kernel<<<split_grid(m), 256, 0, s>>>(m, n, alpha, c, bias, relu);
+        return cuda_status(cudaGetLastError(), "sgemm k=0");
+    }
+    if (mode == ZG_GEMM_SIMT_FP32) return launch_sgemm_simt(m, n, k, alpha, a, b, c, bias, relu, s);
+    const uint64_t need = ws_layout(mode, m, n, k).total;
+    if (need > 0 && (!workspace || workspace_bytes < need))
+        return set_error(ZG_ERR_DISPATCH,
+                         "sgemm: workspace of %llu bytes needed for %d x %d x %d, got %llu",
+                         (unsigned long long)need, m, n, k, (unsigned long long)workspace_bytes);
+    if (need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+        return set_error(ZG_ERR_DISPATCH, "sgemm: workspace must be 256-byte aligned");
+    return sgemm_tensor_core(mode, m, n, k, alpha, a, b, c, bias, relu,
+                             static_cast<uint8_t*>(workspace), s);
+}
+
+extern "C" int zg_kernel_status(uint32_t* code) {
+    uint32_t v = 0, zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_status, sizeof(v));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_status, &zero, sizeof(zero));
+    if (code) *code = v;
+    return cuda_status(e, "zg_kernel_status");
+}

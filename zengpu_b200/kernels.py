@@ -1,0 +1,120 @@
+"""Stream-level entry points on torch CUDA tensors (layer 3 of the C ABI).
+
+Thin wrappers: shape / dtype / device checks in Python, then one call into
+libzengpu_b200 with raw device pointers and torch's current CUDA stream.
+torch only supplies device memory and streams here; every kernel that runs
+is this library's own sm_100a code.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib as L
+from .api import GemmMode, check
+
+_workspaces: dict[int, torch.Tensor] = {}
+
+
+def _stream(t: torch.Tensor) -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _f32_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t.dtype != torch.float32 or not t.is_cuda or not t.is_contiguous():
+            raise ValueError("expected contiguous float32 CUDA tensors")
+
+
+def add_f32(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = a + b, elementwise (bit-exact f32)."""
+    _f32_cuda(a, b)
+    if a.shape != b.shape:
+        raise ValueError(f"add: shape mismatch {tuple(a.shape)} vs {tuple(b.shape)}")
+    out = torch.empty_like(a) if out is None else out
+    _f32_cuda(out)
+    check(L.load().zg_add_f32(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.numel(), _stream(a)))
+    return out
+
+
+def relu_f32(a: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = relu(a); pass out=a for the in-place form."""
+    _f32_cuda(a)
+    out = torch.empty_like(a) if out is None else out
+    _f32_cuda(out)
+    check(L.load().zg_relu_f32(a.data_ptr(), out.data_ptr(), a.numel(), _stream(a)))
+    return out
+
+
+def saxpy_f32(alpha: float, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    _f32_cuda(x, y)
+    check(L.load().zg_saxpy_f32(float(alpha), x.data_ptr(), y.data_ptr(), x.numel(), _stream(x)))
+    return y
+
+
+def sscal_f32(alpha: float, x: torch.Tensor) -> torch.Tensor:
+    _f32_cuda(x)
+    check(L.load().zg_sscal_f32(float(alpha), x.data_ptr(), x.numel(), _stream(x)))
+    return x
+
+
+def workspace_bytes(mode: int, m: int, n: int, k: int) -> int:
+    return int(L.load().zg_sgemm_workspace_bytes(int(mode), m, n, k))
+
+
+def workspace_for(device: torch.device, nbytes: int) -> torch.Tensor | None:
+    """Per-device scratch tensor, grown on demand (stream-ordered reuse)."""
+    if nbytes == 0:
+        return None
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _workspaces.get(idx)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        _workspaces[idx] = ws
+    return ws
+
+
+def sgemm(a: torch.Tensor, b: torch.Tensor, mode: int = GemmMode.TF32X3, alpha: float = 1.0,
+          bias: torch.Tensor | None = None, relu: bool = False,
+          out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """C = epilogue(alpha * a @ b) for row-major f32 a [m,k], b [k,n]."""
+    _f32_cuda(a, b)
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
+        raise ValueError(f"sgemm: bad shapes {tuple(a.shape)} @ {tuple(b.shape)}")
+    m, k = a.shape
+    n = b.shape[1]
+    if bias is not None:
+        _f32_cuda(bias)
+        if bias.numel() != n:
+            raise ValueError("sgemm: bias must have n elements")
+    out = torch.empty((m, n), dtype=torch.float32, device=a.device) if out is None else out
+    _f32_cuda(out)
+    need = workspace_bytes(mode, m, n, k)
+    ws = workspace if workspace is not None else workspace_for(a.device, need)
+    ws_ptr = ws.data_ptr() if ws is not None else None
+    ws_len = ws.numel() if ws is not None else 0
+    check(L.load().zg_sgemm_f32(int(mode), m, n, k, float(alpha), a.data_ptr(), b.data_ptr(),
+                                out.data_ptr(), bias.data_ptr() if bias is not None else None,
+                                1 if relu else 0, ws_ptr, ws_len, _stream(a)))
+    return out
+
+
+def fill_uniform(t: torch.Tensor, seed: int, lo: float = -1.0, hi: float = 1.0) -> torch.Tensor:
+    _f32_cuda(t)
+    check(L.load().zg_fill_uniform_f32(t.data_ptr(), t.numel(), int(seed), float(lo), float(hi),
+                                       _stream(t)))
+    return t
+
+
+def fill_normal(t: torch.Tensor, seed: int) -> torch.Tensor:
+    _f32_cuda(t)
+    check(L.load().zg_fill_normal_f32(t.data_ptr(), t.numel(), int(seed), _stream(t)))
+    return t
+
+
+def kernel_status() -> int:
+    """Reads and clears the device status word (0 = every bounded wait finished)."""
+    code = C.c_uint32(0)
+    check(L.load().zg_kernel_status(C.byref(code)))
+    return int(code.value)

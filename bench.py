@@ -1,0 +1,536 @@
+#!/usr/bin/env python
+"""Benchmark of the ZenGPU compute hot path on B200.
+
+Default workload (one JSON line on rank 0):
+  f32 GEMM, 3xTF32 tensor-core mode (fp32-class accuracy), M = N = K = 8192
+  per GPU.  With N GPUs each rank owns an 8192-row block of A and C (weak
+  scaling, M = 8192 * N); B (8192 x 8192) is broadcast from rank 0 over NCCL
+  every step - the path's only exchange - then every rank runs the split
+  pre-pass and the tcgen05 GEMM on its block.
+
+  value       whole-job useful TFLOP/s (2*M*N*K per step over all ranks),
+              device-timed with CUDA events, max over ranks
+  e2e         the same GEMM through the drop-in API (CudaDevice + BufferPool +
+              GemmKernel at N=1; torch tensors + dist at N>1) with host
+              buffers: pinned H2D of A and B, GEMM, D2H of C, every step
+  roofline    the tcgen05 kernel alone against the 3xTF32 ceiling
+  cpu_baseline the CPU backend's algorithm (the oracle's C restatement of
+              zengpu-cpu's loop) on a bounded row sample, all host cores
+  elementwise add (z = x + y) and in-place ReLU on 2^28 f32 (1 GiB each)
+
+--impl reference runs only the CPU backend's algorithm (rank 0; other ranks
+exit at once) on the same metric and prints its own line.
+--workload mlp / sharded run the op_graph_lower MLP chain or the
+32768 x 32768 x 8192 strong-scaling GEMM instead.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "f32 GEMM TFLOP/s at 8192³ (1/2/4/8 B200); add/ReLU HBM GB/s; vs CPU backend"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def env_ranks() -> tuple[int, int, int]:
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+# ---- clocks -------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons over the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-f", self.path], stdout=subprocess.DEVNULL,
+                stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in Path(self.path).read_text().splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[0].isdigit() and int(parts[0]) == self.gpu_index:
+                    rows.append(parts)
+        except OSError:
+            pass
+        finally:
+            if self.path:
+                try:
+                    os.unlink(self.path)
+                except OSError:
+                    pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = sorted({name for r in rows for name, v in zip(self.REASONS, r[5:9])
+                          if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---- CPU backend baseline (the oracle restatement, bench.py's cpu leg only) ------------
+def _oracle():
+    sys.path.insert(0, str(ROOT / "tests"))
+    import _oracle
+    return _oracle
+
+
+def cpu_gemm_sample(m: int, n: int, k: int, seconds: float, seed: int = 2) -> dict:
+    """Times the CPU backend's row -> col -> k loop (zengpu-cpu via the oracle)
+    on whole rows of C, all host cores, about `seconds` of work."""
+    import numpy as np
+    O = _oracle()
+    threads = os.cpu_count() or 1
+    a = O.uniform(m * k, seed).reshape(m, k)
+    b = O.uniform(k * n, seed + 1000).reshape(k, n)
+    c = np.zeros((m, n), np.float32)
+    L = O.lib()
+
+    def run(rows: int) -> float:
+        t0 = time.perf_counter()
+        L.zgo_sgemm_ref(m, n, k, 1.0, C.c_void_p(a.ctypes.data), C.c_void_p(b.ctypes.data),
+                        C.c_void_p(c.ctypes.data), 0, rows, threads)
+        return time.perf_counter() - t0
+
+    rows = threads
+    dt = run(rows)
+    if dt < seconds / 2:
+        rows = min(m, max(rows, int(rows * seconds / max(dt, 1e-3))))
+        rows = max(threads, rows // threads * threads)
+        dt = run(rows)
+    flops = 2.0 * rows * n * k
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
+            "seconds": dt, "rows": rows,
+            "sample": f"{rows} of {m} rows of C = A@B, {m}x{n}x{k} f32 (row,col,k loop of "
+                      f"zengpu-cpu, unfused mul+add), {threads} threads, {dt:.1f} s"}
+
+
+# ---- GPU helpers ------------------------------------------------------------------------
+def elementwise_bench(torch, K, peak_gbs: float, iters: int = 20) -> dict:
+    n = 1 << 28
+    x = torch.empty(n, device="cuda")
+    y = torch.empty(n, device="cuda")
+    z = torch.empty(n, device="cuda")
+    K.fill_normal(x, 1)
+    K.fill_normal(y, 2)
+    s = torch.cuda.current_stream()
+    out = {}
+    for name, fn, bytes_per in (("add", lambda: K.add_f32(x, y, z), 12),
+                                ("relu_inplace", lambda: K.relu_f32(z, z), 8)):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(iters):
+            fn()
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        gbs = bytes_per * n / (ms * 1e-3) / 1e9
+        out[name] = {"gbs": round(gbs, 1), "ms": round(ms, 4), "frac": round(gbs / peak_gbs, 3),
+                     "bytes": bytes_per * n}
+    out["elements"] = n
+    out["peak_gbs"] = peak_gbs
+    del x, y, z
+    torch.cuda.empty_cache()
+    return out
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["gemm", "mlp", "sharded"], default="gemm")
+    ap.add_argument("--mode", choices=["tf32x3", "tf32", "simt"], default="tf32x3")
+    ap.add_argument("--size", type=int, default=8192)
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the e2e / elementwise / cpu-baseline legs")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    rank, local_rank, world = env_ranks()
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+    return ours(args, rank, local_rank, world)
+
+
+def reference_arm(args, rank: int, world: int) -> int:
+    """The CPU backend's own algorithm, timed on the host cores (rank 0 only)."""
+    if rank != 0:
+        return 0
+    m = n = k = args.size
+    sample = None
+    for _ in range(args.warmup):
+        cpu_gemm_sample(m, n, k, seconds=2.0)
+    vals, secs = [], 0.0
+    for _ in range(args.steps):
+        sample = cpu_gemm_sample(m, n, k, seconds=2.0)
+        vals.append(sample["value"])
+        secs += sample["seconds"]
+    value = statistics.mean(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * secs / max(args.steps, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"sgemm f32 M=N=K={m}, CPU backend loop on a row sample",
+                   "m": m, "n": n, "k": k},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": sample["cores"],
+                         "kind": "port", "sample": sample["sample"]},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def ours(args, rank: int, local_rank: int, world: int) -> int:
+    import torch
+    import torch.distributed as dist
+
+    import zengpu_b200 as zg
+    from zengpu_b200 import kernels as K
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=dev)
+    peaks, peak_src = load_peaks()
+    mode = {"tf32x3": zg.GemmMode.TF32X3, "tf32": zg.GemmMode.TF32,
+            "simt": zg.GemmMode.SIMT_FP32}[args.mode]
+    try:
+        if args.workload == "mlp":
+            line = mlp_workload(args, torch, zg, K, mode, peaks, peak_src, world)
+        else:
+            line = gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank,
+                                 local_rank, world)
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+    return 0
+
+
+def _max_over_ranks(torch, dist, world, value: float) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_rank, world):
+    s = args.size
+    if args.workload == "sharded":
+        m_total, n, k = 32768, 32768, 8192
+        from zengpu_b200.dist import row_range
+        r0, r1 = row_range(m_total, world, rank)
+        m_local = r1 - r0
+        scaling, workload = "strong", f"sgemm {args.mode} M=N=32768 K=8192 row-sharded over {world}"
+    else:
+        m_local, n, k = s, s, s
+        m_total = s * world
+        scaling = "weak"
+        workload = f"sgemm {args.mode} M=N=K={s} per GPU (M={m_total} total, A/C row blocks)"
+
+    a = torch.empty((m_local, k), device="cuda")
+    b = torch.empty((k, n), device="cuda")
+    c = torch.empty((m_local, n), device="cuda")
+    K.fill_uniform(a, 2 + 7919 * rank)
+    if rank == 0:
+        K.fill_uniform(b, 1002)
+    else:
+        b.zero_()
+    ws_bytes = K.workspace_bytes(mode, m_local, n, k)
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device="cuda")
+    lib = zg.load_library()
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+
+    def check(rc):
+        zg.api.check(rc)
+
+    def step(ev0=None, ev1=None):
+        if world > 1:
+            dist.broadcast(b, src=0)
+        check(lib.zg_sgemm_prepare(int(mode), m_local, n, k, a.data_ptr(), b.data_ptr(),
+                                   ws.data_ptr(), ws.numel(), sp))
+        if ev0 is not None:
+            ev0.record(stream)
+        check(lib.zg_sgemm_compute(int(mode), m_local, n, k, 1.0, a.data_ptr(), b.data_ptr(),
+                                   c.data_ptr(), None, 0, ws.data_ptr(), ws.numel(), sp))
+        if ev1 is not None:
+            ev1.record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if K.kernel_status() != 0:
+        raise RuntimeError("bounded on-device wait expired during warm-up")
+
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for i in range(args.steps):
+            step(*kev[i])
+        t1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms_local = t0.elapsed_time(t1) / args.steps
+    kern_ms_local = statistics.mean(e0.elapsed_time(e1) for e0, e1 in kev)
+    ms = _max_over_ranks(torch, dist, world, ms_local)
+    kern_ms = _max_over_ranks(torch, dist, world, kern_ms_local)
+    if K.kernel_status() != 0:
+        raise RuntimeError("bounded on-device wait expired during timing")
+
+    total_flops = 2.0 * m_total * n * k
+    value = total_flops / (ms * 1e-3) / 1e12
+    rank_flops = 2.0 * m_local * n * k
+    achieved = rank_flops / (kern_ms * 1e-3) / 1e12
+    tf32_peak = peaks["bf16_tflops"] / 2.0
+    fp32_simt_peak = 148 * 128 * 2 * 1.965e9 / 1e12  # SMs x FP32 lanes x FMA x max clock
+    peak = {zg.GemmMode.TF32X3: tf32_peak / 3.0, zg.GemmMode.TF32: tf32_peak,
+            zg.GemmMode.SIMT_FP32: fp32_simt_peak}[mode]
+    # TF32X3: split(A) + transpose-split(B) + tcgen05 kernel; TF32: transpose(B)
+    # (+ a pitched copy of A when k % 4 != 0) + tcgen05 kernel; SIMT: one kernel.
+    launches_per_step = {zg.GemmMode.TF32X3: 3, zg.GemmMode.TF32: 2 + (k % 4 != 0),
+                         zg.GemmMode.SIMT_FP32: 1}[mode]
+
+    extras = {}
+    e2e = None
+    cpu = None
+    if not args.no_extras:
+        del ws
+        torch.cuda.empty_cache()
+        e2e = gemm_e2e(args, torch, dist, zg, K, mode, m_local, n, k, m_total, world, local_rank)
+        extras["elementwise"] = elementwise_bench(torch, K, peaks["hbm_gbs"])
+        if world == 1 and rank == 0:
+            cpu = cpu_gemm_sample(m_total, n, k, seconds=12.0)
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: A, B uniform[-1,1) from the splitmix64 generator (seeds 2, 1002)",
+        "config": {"workload": workload, "m": m_total, "n": n, "k": k, "mode": args.mode,
+                   "parallelism": f"dp{world} (A/C row blocks, B broadcast over NCCL)",
+                   "l2": "inputs larger than L2: A, B 256 MiB each, plus 1 GiB of hi/lo planes"},
+        "roofline": {"bound": "tensor" if mode != zg.GemmMode.SIMT_FP32 else "fp32",
+                     "kernel": f"sgemm_tc_kernel<{2 if mode == 1 else 1}>"
+                     if mode != zg.GemmMode.SIMT_FP32 else "sgemm_simt_kernel",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "kernel_ms": kern_ms,
+                     "peak_basis": (f"{peak_src} bf16 {peaks['bf16_tflops']} TFLOP/s / 2 (tf32 "
+                                    "rate)" + (" / 3 (MMAs per useful product)"
+                                               if mode == zg.GemmMode.TF32X3 else ""))
+                     if mode != zg.GemmMode.SIMT_FP32 else
+                     "nominal FP32 SIMT: 148 SMs x 128 lanes x 2 flop x 1965 MHz"},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    if cpu is not None:
+        line["cpu_baseline"] = {"value": cpu["value"], "unit": cpu["unit"], "cores": cpu["cores"],
+                                "kind": "port", "sample": cpu["sample"]}
+    line.update(extras)
+    return line
+
+
+def gemm_e2e(args, torch, dist, zg, K, mode, m_local, n, k, m_total, world, local_rank):
+    """The GEMM through the drop-in API with host buffers, H2D + D2H every step."""
+    ha = torch.empty((m_local, k), pin_memory=True)
+    hb = torch.empty((k, n), pin_memory=True)
+    hc = torch.empty((m_local, n), pin_memory=True)
+    tmp = torch.empty((m_local, k), device="cuda")
+    K.fill_uniform(tmp, 2)
+    ha.copy_(tmp)
+    tmp = torch.empty((k, n), device="cuda")
+    K.fill_uniform(tmp, 1002)
+    hb.copy_(tmp)
+    del tmp
+    torch.cuda.synchronize()
+    steps = max(3, min(args.steps, 5))
+    h2d = ha.numel() * 4 + hb.numel() * 4
+    d2h = hc.numel() * 4
+    if world == 1:
+        device = zg.CudaDevice(local_rank)
+        pool = zg.BufferPool(device)
+        gemm = zg.GemmKernel(device, mode)
+        da = pool.alloc([m_local, k])
+        db = pool.alloc([k, n])
+
+        def step():
+            device.write_buffer_ptr(da.buffer, 0, ha.data_ptr(), ha.numel() * 4)
+            device.write_buffer_ptr(db.buffer, 0, hb.data_ptr(), hb.numel() * 4)
+            out = gemm.gemm(device, pool, da, db)
+            device.read_buffer_ptr(out.buffer, 0, hc.data_ptr(), d2h)
+            pool.free(out)
+
+        for _ in range(2):
+            step()
+        t = time.perf_counter()
+        for _ in range(steps):
+            step()
+        dt = (time.perf_counter() - t) / steps
+        pool.close()
+        device.close()
+        clock = "host clock around synchronous API calls"
+    else:
+        a = torch.empty((m_local, k), device="cuda")
+        b = torch.empty((k, n), device="cuda")
+        from zengpu_b200.dist import ShardedGemm
+        sg = ShardedGemm(mode=int(mode))
+        rank = dist.get_rank()
+        stream = torch.cuda.current_stream()
+
+        def step():
+            a.copy_(ha, non_blocking=True)
+            if rank == 0:
+                b.copy_(hb, non_blocking=True)
+            c = sg.sgemm_rows(a, b, src=0)
+            hc.copy_(c, non_blocking=True)
+
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        dt = _max_over_ranks(torch, dist, world, e0.elapsed_time(e1) / steps / 1e3)
+        h2d = ha.numel() * 4 + (hb.numel() * 4 if rank == 0 else 0)
+        clock = "CUDA events on the compute stream, max over ranks"
+    total_flops = 2.0 * m_total * n * k
+    return {"value": total_flops / dt / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": dt * 1e3, "steps": steps, "clock": clock}
+
+
+def mlp_workload(args, torch, zg, K, mode, peaks, peak_src, world):
+    """op_graph_lower MLP: 4 x (Y = ReLU(X @ W + b)), batch 4096, hidden 4096;
+    fused epilogue vs the unfused gemm -> add(broadcast bias) -> relu chain."""
+    import math
+    bsz = hid = 4096
+    layers = 4
+    x = torch.empty((bsz, hid), device="cuda")
+    K.fill_normal(x, 3)
+    bound = math.sqrt(6.0 / hid)
+    ws = [K.fill_uniform(torch.empty((hid, hid), device="cuda"), 100 + i, -bound, bound)
+          for i in range(layers)]
+    bs = [K.fill_uniform(torch.empty(hid, device="cuda"), 200 + i, -0.1, 0.1)
+          for i in range(layers)]
+    bfull = [b.expand(bsz, hid).contiguous() for b in bs]
+    acts = [torch.empty((bsz, hid), device="cuda") for _ in range(2)]
+    tmp = torch.empty((bsz, hid), device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def fused():
+        h = x
+        for i in range(layers):
+            o = acts[i % 2]
+            K.sgemm(h, ws[i], mode=mode, bias=bs[i], relu=True, out=o)
+            h = o
+        return h
+
+    def unfused():
+        h = x
+        for i in range(layers):
+            o = acts[i % 2]
+            K.sgemm(h, ws[i], mode=mode, out=tmp)
+            K.add_f32(tmp, bfull[i], o)
+            K.relu_f32(o, o)
+            h = o
+        return h
+
+    res = {}
+    for name, fn in (("fused", fused), ("unfused", unfused)):
+        for _ in range(args.warmup):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) / args.steps
+    flops = layers * 2.0 * bsz * hid * hid
+    return {
+        "metric": METRIC, "value": flops / (res["fused"] * 1e-3) / 1e12, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": res["fused"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"op_graph_lower MLP 4 x relu(X@W+b), 4096x4096, {args.mode}",
+                   "unfused_ms_per_step": res["unfused"],
+                   "speedup_fused_vs_unfused": res["unfused"] / res["fused"]},
+        "gpu_launches": args.steps * layers * (3 if mode == 1 else 1),
+    }
+
+
+if __name__ == "__main__":
+    sys.exit(main())

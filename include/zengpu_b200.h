@@ -304,6 +304,18 @@ int zg_sgemm_f32(int mode, int m, int n, int k, float alpha, const float *a, con
                  float *c, const float *bias, int relu, void *workspace,
                  uint64_t workspace_bytes, void *stream);
 
+/* The two halves of zg_sgemm_f32, for callers that reuse operands or time
+ * the main kernel alone.  prepare: writes the operand planes of `mode` into
+ * `workspace` (tf32 hi/lo of A and B for TF32X3, pitch-padded copies for
+ * TF32 when k or n is not a multiple of 4; nothing for SIMT).  compute: runs
+ * the GEMM on planes a previous prepare wrote into the same workspace for the
+ * same (mode, m, n, k, a, b); stream order makes the pair safe. */
+int zg_sgemm_prepare(int mode, int m, int n, int k, const float *a, const float *b,
+                     void *workspace, uint64_t workspace_bytes, void *stream);
+int zg_sgemm_compute(int mode, int m, int n, int k, float alpha, const float *a, const float *b,
+                     float *c, const float *bias, int relu, const void *workspace,
+                     uint64_t workspace_bytes, void *stream);
+
 /* Seeded synthetic inputs, bit-identical to the CPU generator:
  * uniform: x = lo + (hi - lo) * (u24 * 2^-24), or exactly u24*2^-23 - 1 when
  * lo = -1, hi = 1; normal: Box-Muller in f64 (may differ from a host libm in

@@ -52,13 +52,14 @@ def test_no_device_is_reported_not_crashed():
 def test_workspace_bytes():
     lib = zg.load_library()
     assert lib.zg_sgemm_workspace_bytes(0, 1024, 1024, 1024) == 0
-    # TF32X3: hi/lo planes of A (m x k) and B (k x n), pitch rounded to 4
+    # TF32X3: hi/lo planes of A (m x k) and of B transposed (n x k), k pitch rounded to 4
     assert lib.zg_sgemm_workspace_bytes(1, 8192, 8192, 8192) == 4 * 8192 * 8192 * 4
     assert lib.zg_sgemm_workspace_bytes(1, 17, 9, 33) == 2 * 256 * ((17 * 36 * 4 + 255) // 256) + \
-        2 * 256 * ((33 * 12 * 4 + 255) // 256)
-    # TF32: copies only when a pitch is not a multiple of 4 floats
-    assert lib.zg_sgemm_workspace_bytes(2, 64, 64, 64) == 0
-    assert lib.zg_sgemm_workspace_bytes(2, 17, 9, 33) > 0
+        2 * 256 * ((9 * 36 * 4 + 255) // 256)
+    # TF32: the K-major copy of B, plus a pitched copy of A when k % 4 != 0
+    assert lib.zg_sgemm_workspace_bytes(2, 64, 64, 64) == 64 * 64 * 4
+    assert lib.zg_sgemm_workspace_bytes(2, 17, 9, 33) == 256 * ((17 * 36 * 4 + 255) // 256) + \
+        256 * ((9 * 36 * 4 + 255) // 256)
     assert lib.zg_sgemm_workspace_bytes(1, 0, 5, 5) == 0
 
 

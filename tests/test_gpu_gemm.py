@@ -30,7 +30,7 @@ def run(a: np.ndarray, b: np.ndarray, mode, alpha=1.0, bias=None, relu=False) ->
     return c.cpu().numpy()
 
 
-@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
 def test_gemm_17x33x9_kat_exact(device, pool, kats, mode):
     """zengpu-conformance/tests/devarray_matmul.rs:56-129 through GemmKernel."""
     gemm = zg.GemmKernel(device, mode)
@@ -42,7 +42,7 @@ def test_gemm_17x33x9_kat_exact(device, pool, kats, mode):
     gemm.destroy(device)
 
 
-@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
 def test_op_graph_chain(device, pool, kats, mode):
     """examples/op_graph_lower.rs: Matmul -> Add -> Relu as three dispatches."""
     gemm = zg.GemmKernel(device, mode)
@@ -54,7 +54,7 @@ def test_op_graph_chain(device, pool, kats, mode):
     np.testing.assert_array_equal(bits(zg.download(device, y)), bits(kats["op_graph_8x4x6_y"]))
 
 
-@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
 def test_tiled_and_heavy_patterns(kats, mode):
     c = run(kats["tiled_31x29x23_a"], kats["tiled_31x29x23_b"], mode)
     assert np.max(np.abs(c - kats["tiled_31x29x23_c64"])) < 1e-3
@@ -63,7 +63,7 @@ def test_tiled_and_heavy_patterns(kats, mode):
     assert np.all(np.abs(h - ref) / np.maximum(np.abs(ref), 1.0) <= 0.01)
 
 
-@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
 def test_config0_256_parity(mode):
     """M=N=K=256, A,B uniform[-1,1) seed 0 (one stream, A then B)."""
     ab = O.uniform(2 * 256 * 256, 0)
@@ -72,7 +72,7 @@ def test_config0_256_parity(mode):
     assert O.rel_fro(c, O.sgemm_ref(a, b)) <= TOL[mode]
 
 
-@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
 def test_1024_parity_vs_oracle(mode):
     a = O.uniform(1024 * 1024, 2).reshape(1024, 1024)
     b = O.uniform(1024 * 1024, 102).reshape(1024, 1024)
@@ -82,7 +82,7 @@ def test_1024_parity_vs_oracle(mode):
     assert err <= TOL[mode], err
 
 
-@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
 @pytest.mark.parametrize("size", [2048, 4096])
 def test_large_sampled_vs_fp64(mode, size):
     ta = torch.empty((size, size), device="cuda")
@@ -99,7 +99,7 @@ def test_large_sampled_vs_fp64(mode, size):
         assert O.rel_fro(got, ref) <= TOL[mode]
 
 
-@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
 @pytest.mark.parametrize("m,n,k", [(1, 1, 1), (3, 5, 7), (129, 257, 33), (200, 300, 130),
                                    (130, 70, 1000), (257, 513, 31), (64, 8, 4096)])
 def test_odd_shapes(mode, m, n, k):
@@ -110,7 +110,7 @@ def test_odd_shapes(mode, m, n, k):
         assert O.rel_fro(c, O.sgemm(a, b, alpha)) <= max(TOL[mode], 2e-6)
 
 
-@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
 def test_k_zero(mode):
     a = np.zeros((5, 0), np.float32)
     b = np.zeros((0, 7), np.float32)
@@ -118,7 +118,7 @@ def test_k_zero(mode):
     np.testing.assert_array_equal(bits(c), bits(O.sgemm_ref(a, b, -1.0)))
 
 
-@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
 @pytest.mark.parametrize("m,n,k", [(256, 256, 256), (300, 520, 72)])
 def test_fused_bias_relu(mode, m, n, k):
     a = O.normal(m * k, 3).reshape(m, k)
@@ -130,7 +130,7 @@ def test_fused_bias_relu(mode, m, n, k):
     assert (y >= 0).all() and not np.signbit(y).any()
 
 
-@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
 def test_fused_api_matches_unfused_chain(device, pool, mode):
     m, n, k = 96, 160, 48
     a = O.normal(m * k, 8).reshape(m, k)

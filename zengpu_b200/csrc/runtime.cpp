@@ -283,19 +283,20 @@ namespace {
 
 int set_device(zg_device* dev) { return cuda_status(cudaSetDevice(dev->ordinal), "cudaSetDevice"); }
 
-// Drops completed submissions; frees deferred buffers once none is pending.
-// Caller holds dev->mu.
-void sweep_pending(zg_device* dev) {
+// Releases one submission's in-flight token (zengpu-cuda/src/lib.rs:412-444):
+// a submission counts as in flight until poll/wait observes it complete or it
+// is destroyed, exactly as in the reference, even when the GPU finished
+// earlier.  Deferred frees run once no submission is in flight.  Caller
+// holds dev->mu.
+void release_submission(zg_device* dev, cudaEvent_t ev) {
     auto& p = dev->pending;
-    for (size_t i = 0; i < p.size();) {
-        if (cudaEventQuery(p[i]) == cudaSuccess) {
-            cudaEventDestroy(p[i]);
+    for (size_t i = 0; i < p.size(); ++i)
+        if (p[i] == ev) {
             p[i] = p.back();
             p.pop_back();
-        } else {
-            ++i;
+            break;
         }
-    }
+    cudaEventDestroy(ev);
     if (p.empty() && !dev->deferred_buffers.empty()) {
         for (uint32_t idx : dev->deferred_buffers) {
             Buffer* b = dev->buffers.value_at(idx);  // retired slots keep their value
@@ -306,10 +307,7 @@ void sweep_pending(zg_device* dev) {
     }
 }
 
-bool in_flight(zg_device* dev) {
-    sweep_pending(dev);
-    return !dev->pending.empty();
-}
+bool in_flight(zg_device* dev) { return !dev->pending.empty(); }
 
 int stale(const char* what, zg_handle h, uint32_t actual) {
     return set_error(ZG_ERR_STALE_HANDLE, "%s: stale handle (index %u, generation %u, current %u)",
@@ -876,25 +874,18 @@ extern "C" int zg_submit_batch(zg_device* dev, const zg_dispatch_op* ops, uint32
 
 extern "C" int zg_submission_poll(zg_submission* sub, int* done) {
     if (!sub || !done) return set_error(ZG_ERR_BACKEND, "zg_submission_poll: null argument");
-    if (sub->done) {
-        *done = 1;
-        return ZG_OK;
-    }
-    std::lock_guard<std::recursive_mutex> lk(sub->dev->mu);
-    auto& p = sub->dev->pending;
-    bool still = false;
-    for (cudaEvent_t e : p) still |= (e == sub->event);
-    if (!still) {
-        sub->done = true;
-    } else {
+    if (!sub->done) {
+        std::lock_guard<std::recursive_mutex> lk(sub->dev->mu);
+        cudaSetDevice(sub->dev->ordinal);
         cudaError_t e = cudaEventQuery(sub->event);
         if (e == cudaSuccess) {
             sub->done = true;
-            sweep_pending(sub->dev);
-        } else if (e != cudaErrorNotReady) {
-            return cuda_status(e, "submission poll");
-        } else {
+            release_submission(sub->dev, sub->event);
+            sub->event = nullptr;
+        } else if (e == cudaErrorNotReady) {
             cudaGetLastError();
+        } else {
+            return cuda_status(e, "submission poll");
         }
     }
     *done = sub->done ? 1 : 0;
@@ -920,7 +911,18 @@ extern "C" int zg_submission_wait(zg_submission* sub, uint64_t timeout_ns) {
     }
 }
 
-extern "C" void zg_submission_destroy(zg_submission* sub) { delete sub; }
+// Dropping a pending submission waits for its stream position first, then
+// releases its in-flight token (the reference's Drop for CudaSubmission).
+extern "C" void zg_submission_destroy(zg_submission* sub) {
+    if (!sub) return;
+    if (!sub->done && sub->event) {
+        std::lock_guard<std::recursive_mutex> lk(sub->dev->mu);
+        cudaSetDevice(sub->dev->ordinal);
+        cudaEventSynchronize(sub->event);
+        release_submission(sub->dev, sub->event);
+    }
+    delete sub;
+}
 
 // ======================================================================
 // 2. Array ops

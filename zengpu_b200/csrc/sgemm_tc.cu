@@ -9,15 +9,20 @@
 //           the dropped lo*lo term is ~2^-22 relative, so the result keeps
 //           fp32-class accuracy.  A pre-pass writes the hi/lo planes.
 //
-// Kernel layout (one 128 x 256 output tile per CTA, 192 threads):
-//   warp 0      TMA producer: A tile [128 x BK] K-major and B tile [BK x 256]
-//               N-major (B stays row-major in HBM; the MMA reads it MN-major),
-//               128-byte swizzled, into a STAGES-deep mbarrier ring;
-//   warp 1      allocates 256 TMEM columns (the f32 accumulator, lane = row)
-//               and one thread issues tcgen05.mma, committing each stage back
-//               to the producer and the finished tile to the epilogue;
-//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, alpha / bias /
-//               ReLU in registers, 128-bit stores.
+// Kernel layout (one 128 x 256 output tile per CTA, 320 threads):
+//   warp 0      TMA producer: A tile [128 x BK] and B^T tile [256 x BK], both
+//               K-major and swizzled (B is transposed to K-major planes by the
+//               pre-pass), into a STAGES-deep mbarrier ring;
+//   warp 1      allocates 512 TMEM columns (two 128 x 256 f32 accumulators,
+//               lane = row) and one thread issues tcgen05.mma, committing each
+//               stage back to the producer and each finished k-chunk to the
+//               epilogue;
+//   warps 2-9   epilogue: two warps per TMEM lane quarter, one per 128-column
+//               half.  The tensor core's f32 accumulation truncates, so its
+//               error grows with k; the epilogue therefore drains the TMEM
+//               accumulator every kChunkK of k into f32 registers (round to
+//               nearest) while the MMA fills the other accumulator, then
+//               applies alpha / bias / ReLU and stores with 128-bit writes.
 // Every mbarrier wait is bounded (zg_common.cuh); an expiry sets a bit in the
 // device status word, the kernel drains its in-flight copies and MMAs, frees
 // TMEM and returns.
@@ -41,22 +46,25 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BN = 256;
-constexpr int kChunk = 32;  // f32 columns per 128-byte swizzle row
-constexpr int kTcThreads = 192;
-constexpr uint32_t kTmemCols = 256;
+constexpr int kEpiWarps = 8;
+constexpr int kTcThreads = 64 + 32 * kEpiWarps;  // producer, MMA, 8 epilogue warps
+constexpr uint32_t kTmemCols = 512;              // two BN-column accumulators
 
 template <int kPlanes>
 struct TcCfg {
-    static constexpr int BK = kPlanes == 1 ? 32 : 16;      // k per stage
-    static constexpr int STAGES = 4;                       // 48 KB per stage
-    static constexpr int A_BYTES = BM * BK * 4;            // one plane
-    static constexpr int B_CHUNK_BYTES = BK * kChunk * 4;  // one 32-col chunk
-    static constexpr int B_BYTES = BN * BK * 4;            // one plane
+    static constexpr int BK = kPlanes == 1 ? 32 : 16;  // k per stage
+    static constexpr int STAGES = 4;                   // 48 KB per stage
+    static constexpr int A_BYTES = BM * BK * 4;        // one plane
+    static constexpr int B_BYTES = BN * BK * 4;        // one plane
     static constexpr int STAGE_BYTES = kPlanes * (A_BYTES + B_BYTES);
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*bars*/;
-    // A descriptor: K-major, swizzle width = BK*4 bytes (128B or 64B).
-    static constexpr uint32_t A_LAYOUT = BK == 32 ? 2u : 4u;  // SWIZZLE_128B : SWIZZLE_64B
-    static constexpr uint32_t A_SBO = 8 * BK * 4;             // 8-row core-matrix group
+    // Both operands K-major, rows of BK*4 bytes, swizzled at that width.
+    static constexpr uint32_t LAYOUT = BK == 32 ? 2u : 4u;  // SWIZZLE_128B : SWIZZLE_64B
+    static constexpr uint32_t SBO = 8 * BK * 4;             // 8-row core-matrix group
+    // k-blocks per TMEM accumulation chunk: 512 of k for TF32X3 (keeps the
+    // truncation error of the tensor-core accumulator near 3e-6 relative);
+    // TF32 (tolerance 5e-3) accumulates the whole k range in TMEM.
+    static constexpr int KB_PER_CHUNK = kPlanes == 2 ? 512 / BK : (1 << 30);
 };
 
 struct TcMaps {
@@ -74,9 +82,9 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
            (static_cast<uint64_t>(layout) << 61);
 }
 
-// Instruction descriptor, kind::tf32: D f32, A/B tf32, A K-major, B MN-major,
+// Instruction descriptor, kind::tf32: D f32, A/B tf32, both K-major,
 // M = 128, N = 256.
-constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (0u << 15) | (1u << 16) |
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (0u << 15) | (0u << 16) |
                             (static_cast<uint32_t>(BN >> 3) << 17) |
                             (static_cast<uint32_t>(BM >> 4) << 24);
 
@@ -105,8 +113,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                                ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
     uint64_t* empty = full + STAGES;
-    uint64_t* accum_full = empty + STAGES;
-    uint64_t* drain = accum_full + 1;
+    uint64_t* acc_full = empty + STAGES;  // [2]: chunk in TMEM buffer b is complete
+    uint64_t* acc_empty = acc_full + 2;   // [2]: epilogue has drained TMEM buffer b
+    uint64_t* drain = acc_empty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -115,6 +124,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tile_coords(blockIdx.x, mt, nt, m_tile, n_tile);
     const int m0 = m_tile * BM, n0 = n_tile * BN;
     const int nkb = (K + BK - 1) / BK;
+    const int nchunks = (nkb + Cfg::KB_PER_CHUNK - 1) / Cfg::KB_PER_CHUNK;
 
     auto a_plane = [&](int s, int p) { return smem + s * Cfg::STAGE_BYTES + p * Cfg::A_BYTES; };
     auto b_plane = [&](int s, int p) {
@@ -126,7 +136,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(accum_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 32 * kEpiWarps);
+        }
         mbar_init(drain, 1);
         fence_mbar_init();
     }
@@ -154,11 +167,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int k0 = kb * BK;
                 for (int p = 0; p < kPlanes; ++p) {
                     tma_load_2d(a_plane(s, p), &maps.a[p], k0, m0, &full[s]);
-                    uint8_t* bp = b_plane(s, p);
-#pragma unroll
-                    for (int c = 0; c < BN / kChunk; ++c)
-                        tma_load_2d(bp + c * Cfg::B_CHUNK_BYTES, &maps.b[p], n0 + c * kChunk, k0,
-                                    &full[s]);
+                    tma_load_2d(b_plane(s, p), &maps.b[p], k0, n0, &full[s]);
                 }
                 issued = kb + 1;
             }
@@ -171,79 +180,106 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             bool ok = true;
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % STAGES;
-                const uint32_t ph = (kb / STAGES) & 1;
-                if (!mbar_wait_bounded(&full[s], ph, &g_status, kErrTcMma)) {
+            for (int j = 0; j < nchunks && ok; ++j) {
+                const int buf = j & 1;
+                const uint32_t d_tmem = tmem_base + buf * BN;
+                if (j >= 2 && !mbar_wait_bounded(&acc_empty[buf], ((j >> 1) - 1) & 1, &g_status,
+                                                 kErrTcMma)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(a_plane(s, 0));
-                const uint32_t b0 = smem_u32(b_plane(s, 0));
-#pragma unroll
-                for (int kk = 0; kk < BK / 8; ++kk) {
-                    // A: advance 8 f32 (32 bytes) inside the swizzle row.
-                    // B: advance one 8-row (1024-byte) core-matrix group.
-                    const uint64_t ahi = umma_desc(a0 + kk * 32, 16, Cfg::A_SBO, Cfg::A_LAYOUT);
-                    const uint64_t bhi =
-                        umma_desc(b0 + kk * 1024, Cfg::B_CHUNK_BYTES, 1024, 2u);
-                    const uint32_t acc0 = (kb | kk) != 0;
-                    if (kPlanes == 2) {
-                        const uint32_t a1 = smem_u32(a_plane(s, 1));
-                        const uint32_t b1 = smem_u32(b_plane(s, 1));
-                        const uint64_t alo =
-                            umma_desc(a1 + kk * 32, 16, Cfg::A_SBO, Cfg::A_LAYOUT);
-                        const uint64_t blo =
-                            umma_desc(b1 + kk * 1024, Cfg::B_CHUNK_BYTES, 1024, 2u);
-                        mma_tf32_ss(tmem_base, alo, bhi, kIdesc, acc0);
-                        mma_tf32_ss(tmem_base, ahi, blo, kIdesc, 1u);
-                        mma_tf32_ss(tmem_base, ahi, bhi, kIdesc, 1u);
-                    } else {
-                        mma_tf32_ss(tmem_base, ahi, bhi, kIdesc, acc0);
+                const int kb0 = j * Cfg::KB_PER_CHUNK;
+                const int kb1 = min(nkb, kb0 + Cfg::KB_PER_CHUNK);
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    const int s = kb % STAGES;
+                    const uint32_t ph = (kb / STAGES) & 1;
+                    if (!mbar_wait_bounded(&full[s], ph, &g_status, kErrTcMma)) {
+                        ok = false;
+                        break;
                     }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(a_plane(s, 0));
+                    const uint32_t b0 = smem_u32(b_plane(s, 0));
+#pragma unroll
+                    for (int kk = 0; kk < BK / 8; ++kk) {
+                        // Advance 8 f32 (32 bytes) inside the swizzled K row.
+                        const uint64_t ahi = umma_desc(a0 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
+                        const uint64_t bhi = umma_desc(b0 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
+                        const uint32_t acc0 = (kb != kb0 || kk != 0) ? 1u : 0u;
+                        if (kPlanes == 2) {
+                            const uint32_t a1 = smem_u32(a_plane(s, 1));
+                            const uint32_t b1 = smem_u32(b_plane(s, 1));
+                            const uint64_t alo =
+                                umma_desc(a1 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
+                            const uint64_t blo =
+                                umma_desc(b1 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
+                            mma_tf32_ss(d_tmem, alo, bhi, kIdesc, acc0);
+                            mma_tf32_ss(d_tmem, ahi, blo, kIdesc, 1u);
+                            mma_tf32_ss(d_tmem, ahi, bhi, kIdesc, 1u);
+                        } else {
+                            mma_tf32_ss(d_tmem, ahi, bhi, kIdesc, acc0);
+                        }
+                    }
+                    mma_commit(&empty[s]);  // stage s free once these MMAs finish
                 }
-                mma_commit(&empty[s]);  // stage s free once these MMAs finish
+                if (ok) mma_commit(&acc_full[buf]);  // chunk j complete in buffer buf
             }
-            if (ok) {
-                mma_commit(accum_full);
-            } else {
+            if (!ok) {
                 mma_commit(drain);
                 mbar_wait_bounded(drain, 0, &g_status, kErrTcDrain);
             }
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
-        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        // ---------------- epilogue (warps 2..9) ----------------
+        const int q = warp & 3;                 // TMEM lane quarter this warp may access
+        const int half = (warp - 2) >> 2;        // 128-column half of the tile
         const int row = m0 + q * 32 + lane;
-        const bool ok = mbar_wait_bounded(accum_full, 0, &g_status, kErrTcEpilogue);
-        tc_fence_after();
-        if (ok) {
-#pragma unroll 1
-            for (int cc = 0; cc < BN / 32; ++cc) {
-                const int col0 = n0 + cc * 32;
-                if (col0 >= N) break;
+        const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + half * 128;
+        float acc[128];
+#pragma unroll
+        for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < nchunks; ++j) {
+            const int buf = j & 1;
+            if (!mbar_wait_bounded(&acc_full[buf], (j >> 1) & 1, &g_status, kErrTcEpilogue)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
                 uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + cc * 32, r);
-                if (row < M) {
+                tmem_ld_32x32b_x32(lane_base + buf * BN + cc * 32, r);
+#pragma unroll
+                for (int t = 0; t < 32; ++t) acc[cc * 32 + t] += __uint_as_float(r[t]);
+            }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[buf]);
+        }
+        if (ok && row < M) {
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                const int col0 = n0 + half * 128 + cc * 32;
+                if (col0 < N) {
                     float v[32];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        float x = __fmul_rn(alpha, __uint_as_float(r[j]));
-                        if (bias) x = __fadd_rn(x, col0 + j < N ? __ldg(bias + col0 + j) : 0.0f);
+                    for (int t = 0; t < 32; ++t) {
+                        float x = __fmul_rn(alpha, acc[cc * 32 + t]);
+                        if (bias) x = __fadd_rn(x, col0 + t < N ? __ldg(bias + col0 + t) : 0.0f);
                         if (relu) x = relu1(x);
-                        v[j] = x;
+                        v[t] = x;
                     }
                     float* dst = C + static_cast<size_t>(row) * N + col0;
                     if (vec_c && col0 + 32 <= N) {
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4*>(dst + j) =
-                                make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        for (int t = 0; t < 32; t += 4)
+                            *reinterpret_cast<float4*>(dst + t) =
+                                make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
                     } else {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (col0 + j < N) dst[j] = v[j];
+                        for (int t = 0; t < 32; ++t)
+                            if (col0 + t < N) dst[t] = v[t];
                     }
                 }
             }
@@ -291,6 +327,36 @@ __global__ void __launch_bounds__(256)
             h[c] = xh;
             l[c] = make_float4(to_tf32(__fsub_rn(x.x, xh.x)), to_tf32(__fsub_rn(x.y, xh.y)),
                                to_tf32(__fsub_rn(x.z, xh.z)), to_tf32(__fsub_rn(x.w, xh.w)));
+        }
+    }
+}
+
+// Transposing variant for B: dst[n, k] = f(src[k, n]) from a K x N source
+// (pitch lds) into N x K planes (pitch ldd), through a 32 x 33 shared tile so
+// both the reads and the writes are coalesced.  hi = tf32(x) (round) or x;
+// lo = tf32(x - hi) when `lo` is non-null.
+__global__ void __launch_bounds__(256)
+    transpose_planes_kernel(const float* __restrict__ src, int K, int N, int64_t lds,
+                            float* __restrict__ hi, float* __restrict__ lo, int64_t ldd,
+                            int round) {
+    __shared__ float tile[32][33];
+    const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+#pragma unroll
+    for (int j = ty; j < 32; j += 8) {
+        const int k = k0 + j, n = n0 + tx;
+        tile[j][tx] = (k < K && n < N) ? __ldcs(src + static_cast<int64_t>(k) * lds + n) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = ty; j < 32; j += 8) {
+        const int n = n0 + j, k = k0 + tx;
+        if (n < N && k < K) {
+            const float x = tile[tx][j];
+            const float h = round ? to_tf32(x) : x;
+            const int64_t o = static_cast<int64_t>(n) * ldd + k;
+            hi[o] = h;
+            if (lo) lo[o] = to_tf32(__fsub_rn(x, h));
         }
     }
 }
@@ -353,9 +419,10 @@ constexpr uint64_t kNone = ~0ull;
 
 WsLayout ws_layout(int mode, int m, int n, int k) {
     WsLayout w{kNone, kNone, kNone, kNone, 0};
-    const uint64_t kp = round_up(k, 4), np = round_up(n, 4);
+    // A planes M x kp, B planes (transposed, K-major) N x kp.
+    const uint64_t kp = round_up(k, 4);
     const uint64_t a_bytes = round_up(static_cast<uint64_t>(m) * kp * 4, 256);
-    const uint64_t b_bytes = round_up(static_cast<uint64_t>(k) * np * 4, 256);
+    const uint64_t b_bytes = round_up(static_cast<uint64_t>(n) * kp * 4, 256);
     uint64_t off = 0;
     if (mode == ZG_GEMM_TF32X3) {
         w.a_hi = off; off += a_bytes;
@@ -364,7 +431,7 @@ WsLayout ws_layout(int mode, int m, int n, int k) {
         w.b_lo = off; off += b_bytes;
     } else if (mode == ZG_GEMM_TF32) {
         if (k % 4 != 0) { w.a_hi = off; off += a_bytes; }
-        if (n % 4 != 0) { w.b_hi = off; off += b_bytes; }
+        w.b_hi = off; off += b_bytes;
     }
     w.total = off;
     return w;
@@ -395,6 +462,16 @@ int launch_split(const float* src, int rows, int cols, int64_t lds, float* hi, f
     return cuda_status(cudaGetLastError(), "sgemm split pre-pass");
 }
 
+// Writes the K-major (transposed) planes of B: N x K, pitch ldd.
+int launch_transpose(const float* src, int K, int N, int64_t lds, float* hi, float* lo,
+                     int64_t ldd, int round, cudaStream_t s) {
+    if (K == 0 || N == 0) return ZG_OK;
+    dim3 grid((N + 31) / 32, (K + 31) / 32);
+    if (grid.y > 65535u) return set_error(ZG_ERR_DISPATCH, "sgemm: k too large for the pre-pass");
+    transpose_planes_kernel<<<grid, 256, 0, s>>>(src, K, N, lds, hi, lo, ldd, round);
+    return cuda_status(cudaGetLastError(), "sgemm transpose pre-pass");
+}
+
 template <int kPlanes>
 int launch_tc(const TcMaps& maps, int M, int N, int K, float alpha, float* C, const float* bias,
               int relu, cudaStream_t s) {
@@ -414,60 +491,88 @@ int launch_tc(const TcMaps& maps, int M, int N, int K, float alpha, float* C, co
     return cuda_status(cudaGetLastError(), "sgemm_tc");
 }
 
-int sgemm_tensor_core(int mode, int M, int N, int K, float alpha, const float* A, const float* B,
-                      float* C, const float* bias, int relu, uint8_t* ws, cudaStream_t s) {
+// Writes the planes the tensor-core kernel reads: tf32 hi/lo of A and B
+// (TF32X3), or pitch-padded copies (TF32 with k or n not a multiple of 4).
+int prepare_planes(int mode, int M, int N, int K, const float* A, const float* B, uint8_t* ws,
+                   cudaStream_t s) {
     const WsLayout w = ws_layout(mode, M, N, K);
     const int64_t kp = static_cast<int64_t>(round_up(K, 4));
-    const int64_t np = static_cast<int64_t>(round_up(N, 4));
+    int rc = ZG_OK;
+    if (mode == ZG_GEMM_TF32X3) {
+        if ((rc = launch_split(A, M, K, K, reinterpret_cast<float*>(ws + w.a_hi),
+                               reinterpret_cast<float*>(ws + w.a_lo), kp, 1, s)) != ZG_OK)
+            return rc;
+        return launch_transpose(B, K, N, N, reinterpret_cast<float*>(ws + w.b_hi),
+                                reinterpret_cast<float*>(ws + w.b_lo), kp, 1, s);
+    }
+    if (mode == ZG_GEMM_TF32) {
+        if (w.a_hi != kNone &&
+            (rc = launch_split(A, M, K, K, reinterpret_cast<float*>(ws + w.a_hi), nullptr, kp, 0,
+                               s)) != ZG_OK)
+            return rc;
+        rc = launch_transpose(B, K, N, N, reinterpret_cast<float*>(ws + w.b_hi), nullptr, kp, 0, s);
+    }
+    return rc;
+}
+
+// Encodes the tensor maps over the prepared planes (or the raw operands) and
+// launches the tcgen05 kernel.
+int compute_planes(int mode, int M, int N, int K, float alpha, const float* A, const float* B,
+                   float* C, const float* bias, int relu, const uint8_t* ws, cudaStream_t s) {
+    (void)B;
+    const WsLayout w = ws_layout(mode, M, N, K);
+    const int64_t kp = static_cast<int64_t>(round_up(K, 4));
     TcMaps maps;
     std::memset(&maps, 0, sizeof(maps));
     int rc;
+    auto plane = [&](uint64_t off) { return reinterpret_cast<const float*>(ws + off); };
     if (mode == ZG_GEMM_TF32X3) {
-        float* ahi = reinterpret_cast<float*>(ws + w.a_hi);
-        float* alo = reinterpret_cast<float*>(ws + w.a_lo);
-        float* bhi = reinterpret_cast<float*>(ws + w.b_hi);
-        float* blo = reinterpret_cast<float*>(ws + w.b_lo);
-        if ((rc = launch_split(A, M, K, K, ahi, alo, kp, 1, s)) != ZG_OK) return rc;
-        if ((rc = launch_split(B, K, N, N, bhi, blo, np, 1, s)) != ZG_OK) return rc;
-        const CUtensorMapSwizzle aswz = TcCfg<2>::BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B
-                                                            : CU_TENSOR_MAP_SWIZZLE_64B;
-        if ((rc = encode_map(&maps.a[0], ahi, K, M, kp, TcCfg<2>::BK, BM, aswz)) != ZG_OK) return rc;
-        if ((rc = encode_map(&maps.a[1], alo, K, M, kp, TcCfg<2>::BK, BM, aswz)) != ZG_OK) return rc;
-        if ((rc = encode_map(&maps.b[0], bhi, N, K, np, kChunk, TcCfg<2>::BK,
-                             CU_TENSOR_MAP_SWIZZLE_128B)) != ZG_OK)
-            return rc;
-        if ((rc = encode_map(&maps.b[1], blo, N, K, np, kChunk, TcCfg<2>::BK,
-                             CU_TENSOR_MAP_SWIZZLE_128B)) != ZG_OK)
-            return rc;
+        using Cfg = TcCfg<2>;
+        const CUtensorMapSwizzle swz =
+            Cfg::BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+        if ((rc = encode_map(&maps.a[0], plane(w.a_hi), K, M, kp, Cfg::BK, BM, swz))) return rc;
+        if ((rc = encode_map(&maps.a[1], plane(w.a_lo), K, M, kp, Cfg::BK, BM, swz))) return rc;
+        if ((rc = encode_map(&maps.b[0], plane(w.b_hi), K, N, kp, Cfg::BK, BN, swz))) return rc;
+        if ((rc = encode_map(&maps.b[1], plane(w.b_lo), K, N, kp, Cfg::BK, BN, swz))) return rc;
         return launch_tc<2>(maps, M, N, K, alpha, C, bias, relu, s);
     }
-    // TF32: raw operands, or pitch-padded copies when a pitch is not 16-byte aligned.
-    const float* a_src = A;
-    int64_t lda = K;
-    if (w.a_hi != kNone) {
-        float* ap = reinterpret_cast<float*>(ws + w.a_hi);
-        if ((rc = launch_split(A, M, K, K, ap, nullptr, kp, 0, s)) != ZG_OK) return rc;
-        a_src = ap;
-        lda = kp;
-    }
-    const float* b_src = B;
-    int64_t ldb = N;
-    if (w.b_hi != kNone) {
-        float* bp = reinterpret_cast<float*>(ws + w.b_hi);
-        if ((rc = launch_split(B, K, N, N, bp, nullptr, np, 0, s)) != ZG_OK) return rc;
-        b_src = bp;
-        ldb = np;
-    }
-    if (!aligned16(a_src) || !aligned16(b_src))
-        return set_error(ZG_ERR_DISPATCH,
-                         "sgemm (TF32 mode): A and B must start on a 16-byte boundary");
-    if ((rc = encode_map(&maps.a[0], a_src, K, M, lda, TcCfg<1>::BK, BM,
-                         CU_TENSOR_MAP_SWIZZLE_128B)) != ZG_OK)
+    using Cfg = TcCfg<1>;
+    const float* a_src = w.a_hi != kNone ? plane(w.a_hi) : A;
+    const int64_t lda = w.a_hi != kNone ? kp : K;
+    if (!aligned16(a_src))
+        return set_error(ZG_ERR_DISPATCH, "sgemm (TF32 mode): A must start on a 16-byte boundary");
+    if ((rc = encode_map(&maps.a[0], a_src, K, M, lda, Cfg::BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
-    if ((rc = encode_map(&maps.b[0], b_src, N, K, ldb, kChunk, TcCfg<1>::BK,
-                         CU_TENSOR_MAP_SWIZZLE_128B)) != ZG_OK)
+    if ((rc = encode_map(&maps.b[0], plane(w.b_hi), K, N, kp, Cfg::BK, BN,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
     return launch_tc<1>(maps, M, N, K, alpha, C, bias, relu, s);
+}
+
+// Shared argument checks of the three GEMM entry points.  Returns ZG_OK and
+// sets *trivial when there is nothing (m or n is 0) to compute.
+int check_gemm_args(int mode, int m, int n, int k, const float* a, const float* b,
+                    const void* workspace, uint64_t workspace_bytes, bool need_c, const float* c,
+                    bool* trivial) {
+    *trivial = false;
+    if (mode != ZG_GEMM_SIMT_FP32 && mode != ZG_GEMM_TF32X3 && mode != ZG_GEMM_TF32)
+        return set_error(ZG_ERR_DISPATCH, "sgemm: unknown mode %d", mode);
+    if (m < 0 || n < 0 || k < 0)
+        return set_error(ZG_ERR_DISPATCH, "sgemm: negative shape %d x %d x %d", m, n, k);
+    if (m == 0 || n == 0) {
+        *trivial = true;
+        return ZG_OK;
+    }
+    if ((need_c && !c) || (k > 0 && (!a || !b)))
+        return set_error(ZG_ERR_DISPATCH, "sgemm: null operand pointer");
+    const uint64_t need = k > 0 ? ws_layout(mode, m, n, k).total : 0;
+    if (need > 0 && (!workspace || workspace_bytes < need))
+        return set_error(ZG_ERR_DISPATCH,
+                         "sgemm: workspace of %llu bytes needed for %d x %d x %d, got %llu",
+                         (unsigned long long)need, m, n, k, (unsigned long long)workspace_bytes);
+    if (need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+        return set_error(ZG_ERR_DISPATCH, "sgemm: workspace must be 256-byte aligned");
+    return ZG_OK;
 }
 
 }  // namespace
@@ -480,31 +585,39 @@ extern "C" uint64_t zg_sgemm_workspace_bytes(int mode, int m, int n, int k) {
     return ws_layout(mode, m, n, k).total;
 }
 
-extern "C" int zg_sgemm_f32(int mode, int m, int n, int k, float alpha, const float* a,
-                            const float* b, float* c, const float* bias, int relu,
-                            void* workspace, uint64_t workspace_bytes, void* stream) {
-    if (mode != ZG_GEMM_SIMT_FP32 && mode != ZG_GEMM_TF32X3 && mode != ZG_GEMM_TF32)
-        return set_error(ZG_ERR_DISPATCH, "sgemm: unknown mode %d", mode);
-    if (m < 0 || n < 0 || k < 0)
-        return set_error(ZG_ERR_DISPATCH, "sgemm: negative shape %d x %d x %d", m, n, k);
-    if (m == 0 || n == 0) return ZG_OK;
-    if (!c || (k > 0 && (!a || !b)))
-        return set_error(ZG_ERR_DISPATCH, "sgemm: null operand pointer");
+extern "C" int zg_sgemm_prepare(int mode, int m, int n, int k, const float* a, const float* b,
+                                void* workspace, uint64_t workspace_bytes, void* stream) {
+    bool trivial;
+    int rc = check_gemm_args(mode, m, n, k, a, b, workspace, workspace_bytes, false, nullptr,
+                             &trivial);
+    if (rc || trivial || k == 0 || mode == ZG_GEMM_SIMT_FP32) return rc;
+    return prepare_planes(mode, m, n, k, a, b, static_cast<uint8_t*>(workspace),
+                          static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int zg_sgemm_compute(int mode, int m, int n, int k, float alpha, const float* a,
+                                const float* b, float* c, const float* bias, int relu,
+                                const void* workspace, uint64_t workspace_bytes, void* stream) {
+    bool trivial;
+    int rc = check_gemm_args(mode, m, n, k, a, b, workspace, workspace_bytes, true, c, &trivial);
+    if (rc || trivial) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (k == 0) {
         gemm_k0_kernel<<<split_grid(m), 256, 0, s>>>(m, n, alpha, c, bias, relu);
         return cuda_status(cudaGetLastError(), "sgemm k=0");
     }
     if (mode == ZG_GEMM_SIMT_FP32) return launch_sgemm_simt(m, n, k, alpha, a, b, c, bias, relu, s);
-    const uint64_t need = ws_layout(mode, m, n, k).total;
-    if (need > 0 && (!workspace || workspace_bytes < need))
-        return set_error(ZG_ERR_DISPATCH,
-                         "sgemm: workspace of %llu bytes needed for %d x %d x %d, got %llu",
-                         (unsigned long long)need, m, n, k, (unsigned long long)workspace_bytes);
-    if (need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
-        return set_error(ZG_ERR_DISPATCH, "sgemm: workspace must be 256-byte aligned");
-    return sgemm_tensor_core(mode, m, n, k, alpha, a, b, c, bias, relu,
-                             static_cast<uint8_t*>(workspace), s);
+    return compute_planes(mode, m, n, k, alpha, a, b, c, bias, relu,
+                          static_cast<const uint8_t*>(workspace), s);
+}
+
+extern "C" int zg_sgemm_f32(int mode, int m, int n, int k, float alpha, const float* a,
+                            const float* b, float* c, const float* bias, int relu,
+                            void* workspace, uint64_t workspace_bytes, void* stream) {
+    int rc = zg_sgemm_prepare(mode, m, n, k, a, b, workspace, workspace_bytes, stream);
+    if (rc) return rc;
+    return zg_sgemm_compute(mode, m, n, k, alpha, a, b, c, bias, relu, workspace,
+                            workspace_bytes, stream);
 }
 
 extern "C" int zg_kernel_status(uint32_t* code) {

@@ -316,6 +316,21 @@ int zg_sgemm_compute(int mode, int m, int n, int k, float alpha, const float *a,
                      float *c, const float *bias, int relu, const void *workspace,
                      uint64_t workspace_bytes, void *stream);
 
+/* zg_sgemm_f32 for callers that cannot allocate device memory when they call
+ * (no counterpart in the reference: ZenGPU's GemmKernel always allocates its
+ * output from a BufferPool).  For example a host framework that owns all of
+ * HBM in its own pool, a latency-critical loop that cannot pay for cudaMalloc's
+ * device-wide synchronisation, or code inside an allocator callback.  The
+ * caller still passes a, b, c (and bias); instead of a workspace this uses a
+ * fixed 64 MiB scratch array in the library's device image, held on every GPU
+ * that loads it until the process exits.  Shapes whose scratch need
+ * (zg_sgemm_workspace_bytes) exceeds 64 MiB are rejected with ZG_ERR_DISPATCH
+ * (TF32X3 fits up to 2048^3).  Allocates nothing.  The first call on each
+ * device looks up the array's device address (make it before any stream
+ * capture).  All calls share the array: calls that overlap on the GPU race. */
+int zg_sgemm_f32_noalloc(int mode, int m, int n, int k, float alpha, const float *a,
+                         const float *b, float *c, const float *bias, int relu, void *stream);
+
 /* Seeded synthetic inputs, bit-identical to the CPU generator:
  * uniform: x = lo + (hi - lo) * (u24 * 2^-24), or exactly u24*2^-23 - 1 when
  * lo = -1, hi = 1; normal: Box-Muller in f64 (may differ from a host libm in

@@ -140,6 +140,7 @@ SIGNATURES: dict[str, tuple] = {
     "zg_sgemm_f32": (_i, [_i, _i, _i, _i, _f, _fp, _fp, _fp, _fp, _i, _vp, _u64, _vp]),
     "zg_sgemm_prepare": (_i, [_i, _i, _i, _i, _fp, _fp, _vp, _u64, _vp]),
     "zg_sgemm_compute": (_i, [_i, _i, _i, _i, _f, _fp, _fp, _fp, _fp, _i, _vp, _u64, _vp]),
+    "zg_sgemm_f32_noalloc": (_i, [_i, _i, _i, _i, _f, _fp, _fp, _fp, _fp, _i, _vp]),
     "zg_fill_uniform_f32": (_i, [_fp, _u64, _u64, _f, _f, _vp]),
     "zg_fill_normal_f32": (_i, [_fp, _u64, _u64, _vp]),
     "zg_kernel_status": (_i, [C.POINTER(_u32)]),

@@ -43,6 +43,15 @@ sys.path.insert(0, str(ROOT))
 METRIC = "f32 GEMM TFLOP/s at 8192³ (1/2/4/8 B200); add/ReLU HBM GB/s; vs CPU backend"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
+# dominant kernel, from one ncu capture of the same workload on a B200:
+#   --set full -k regex:sgemm_tc_kernel on `bench.py --steps 1 --warmup 3 --no-extras`
+#   --section MemoryWorkloadAnalysis -k regex:stream_vec_kernel on the elementwise workload
+NCU_TRAFFIC = {
+    ("gemm", "tf32x3", 8192): 5.841e9,
+    ("elementwise", "add", 1 << 28): 3.188e9,
+}
+
 
 def load_peaks() -> tuple[dict, str]:
     p = ROOT / "MEASURED_PEAKS.json"
@@ -193,7 +202,8 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["gemm", "mlp", "sharded"], default="gemm")
+    ap.add_argument("--workload", choices=["gemm", "mlp", "sharded", "elementwise"],
+                    default="gemm")
     ap.add_argument("--mode", choices=["tf32x3", "tf32", "simt"], default="tf32x3")
     ap.add_argument("--size", type=int, default=8192)
     ap.add_argument("--no-extras", action="store_true",
@@ -255,6 +265,9 @@ def ours(args, rank: int, local_rank: int, world: int) -> int:
     try:
         if args.workload == "mlp":
             line = mlp_workload(args, torch, zg, K, mode, peaks, peak_src, world)
+        elif args.workload == "elementwise":
+            line = elementwise_workload(args, torch, dist, K, peaks, peak_src, rank, local_rank,
+                                        world)
         else:
             line = gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank,
                                  local_rank, world)
@@ -380,7 +393,10 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
                      "kernel": f"sgemm_tc_kernel<{2 if mode == 1 else 1}>"
                      if mode != zg.GemmMode.SIMT_FP32 else "sgemm_simt_kernel",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": None,
+                     "frac": achieved / peak,
+                     "traffic": NCU_TRAFFIC.get(("gemm", args.mode, s))
+                     if args.workload == "gemm" else None,
+                     "algorithmic_bytes": algorithmic_bytes(mode, m_local, n, k),
                      "kernel_ms": kern_ms,
                      "peak_basis": (f"{peak_src} bf16 {peaks['bf16_tflops']} TFLOP/s / 2 (tf32 "
                                     "rate)" + (" / 3 (MMAs per useful product)"
@@ -397,6 +413,14 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
                                 "kind": "port", "sample": cpu["sample"]}
     line.update(extras)
     return line
+
+
+def algorithmic_bytes(mode: int, m: int, n: int, k: int) -> int:
+    """Bytes the GEMM kernel must move once: its operand planes in, C out."""
+    planes = 2 if mode == 1 else 1
+    if mode == 0:  # SIMT reads A and B directly
+        return 4 * (m * k + k * n + m * n)
+    return 4 * planes * (m * k + n * k) + 4 * m * n
 
 
 def gemm_e2e(args, torch, dist, zg, K, mode, m_local, n, k, m_total, world, local_rank):
@@ -469,6 +493,122 @@ def gemm_e2e(args, torch, dist, zg, K, mode, m_local, n, k, m_total, world, loca
     total_flops = 2.0 * m_total * n * k
     return {"value": total_flops / dt / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": dt * 1e3, "steps": steps, "clock": clock}
+
+
+def elementwise_workload(args, torch, dist, K, peaks, peak_src, rank, local_rank, world):
+    """DeviceArray add (z = x + y) then in-place ReLU on 2^28 f32 per GPU
+    (1 GiB per array, larger than L2); value = whole-job HBM GB/s of the pair
+    (20 algorithmic bytes per element), chunks independent per rank."""
+    n = 1 << 28
+    x = torch.empty(n, device="cuda")
+    y = torch.empty(n, device="cuda")
+    z = torch.empty(n, device="cuda")
+    K.fill_normal(x, 1 + 7919 * rank)
+    K.fill_normal(y, 2 + 7919 * rank)
+    stream = torch.cuda.current_stream()
+
+    def step(ev=None):
+        if ev:
+            ev[0].record(stream)
+        K.add_f32(x, y, z)
+        if ev:
+            ev[1].record(stream)
+        K.relu_f32(z, z)
+        if ev:
+            ev[2].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for i in range(args.steps):
+            step(evs[i])
+        t1.record(stream)
+        torch.cuda.synchronize()
+    ms = _max_over_ranks(torch, dist, world, t0.elapsed_time(t1) / args.steps)
+    add_ms = _max_over_ranks(torch, dist, world,
+                             statistics.mean(e[0].elapsed_time(e[1]) for e in evs))
+    relu_ms = _max_over_ranks(torch, dist, world,
+                              statistics.mean(e[1].elapsed_time(e[2]) for e in evs))
+    peak = peaks["hbm_gbs"]
+    value = 20.0 * n * world / (ms * 1e-3) / 1e9
+    add_gbs = 12.0 * n / (add_ms * 1e-3) / 1e9
+    relu_gbs = 8.0 * n / (relu_ms * 1e-3) / 1e9
+    # e2e: host arrays in pinned memory, H2D of x and y, add + relu, D2H of z
+    hx = torch.empty(n, pin_memory=True)
+    hy = torch.empty(n, pin_memory=True)
+    hz = torch.empty(n, pin_memory=True)
+    hx.copy_(x)
+    hy.copy_(y)
+    torch.cuda.synchronize()
+
+    def e2e_step():
+        x.copy_(hx, non_blocking=True)
+        y.copy_(hy, non_blocking=True)
+        K.add_f32(x, y, z)
+        K.relu_f32(z, z)
+        hz.copy_(z, non_blocking=True)
+
+    e2e_step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(3):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = _max_over_ranks(torch, dist, world, e0.elapsed_time(e1) / 3)
+    cpu = None
+    if world == 1 and rank == 0:
+        cpu = cpu_elementwise(n)
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: x, y normal(0,1), splitmix64 + Box-Muller (seeds 1, 2)",
+        "config": {"workload": "DeviceArray add z=x+y then in-place relu(z), 2^28 f32 per GPU",
+                   "elements_per_gpu": n, "bytes_per_element": 20,
+                   "l2": "inputs larger than L2 (1 GiB per array)",
+                   "parallelism": f"{world} independent contiguous chunks, no collective"},
+        "roofline": {"bound": "hbm", "kernel": "stream_vec_kernel<AddOp>", "achieved": add_gbs,
+                     "peak": peak, "unit": "GB/s", "frac": add_gbs / peak,
+                     "traffic": NCU_TRAFFIC.get(("elementwise", "add", n)),
+                     "algorithmic_bytes": 12 * n,
+                     "kernel_ms": add_ms, "peak_basis": f"{peak_src} hbm_gbs",
+                     "relu_inplace": {"achieved": relu_gbs, "frac": relu_gbs / peak,
+                                      "kernel_ms": relu_ms}},
+        "e2e": {"value": 20.0 * n * world / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": 8 * n, "d2h_bytes_per_step": 4 * n,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    return line
+
+
+def cpu_elementwise(n: int) -> dict:
+    """The CPU backend's add then relu over n elements, all host cores."""
+    O = _oracle()
+    threads = os.cpu_count() or 1
+    x = O.normal(n, 1)
+    y = O.normal(n, 2)
+    reps = 0
+    t = time.perf_counter()
+    while time.perf_counter() - t < 10.0 or reps < 2:
+        z = O.add(x, y, threads=threads)
+        O.relu(z, threads=threads)
+        reps += 1
+    dt = (time.perf_counter() - t) / reps
+    return {"value": 20.0 * n / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"add + relu over all {n} elements, {reps} repetitions, {threads} threads "
+                      "(zengpu-cpu semantics, output buffers freshly allocated per call)"}
 
 
 def mlp_workload(args, torch, zg, K, mode, peaks, peak_src, world):

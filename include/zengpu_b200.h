@@ -270,6 +270,18 @@ int zg_gemm_bias_relu(const zg_gemm_kernel *k, zg_device *dev, zg_pool *pool, fl
                       const zg_device_array *a, const zg_device_array *b,
                       const zg_device_array *bias, zg_device_array *out);
 
+/* GemmKernel::sgemm on host arrays (new; the reference's callers write A and
+ * B, dispatch and read C back, one synchronous step after the other):
+ * C[m,n] = epilogue(alpha * A @ B) with a [m,k], b [k,n], c [m,n] row-major
+ * host pointers and an optional host bias [n] (relu as in zg_sgemm_f32).
+ * B is uploaded first, then row panels of A are uploaded, multiplied and
+ * their C rows downloaded on three streams so the copies in both directions
+ * overlap the tensor-core work.  Synchronous; device staging is cached per
+ * device.  Pinned (page-locked) host memory gives full PCIe bandwidth. */
+int zg_gemm_sgemm_host(const zg_gemm_kernel *k, zg_device *dev, float alpha, const float *a,
+                       const float *b, const float *bias, int relu, float *c, uint32_t m,
+                       uint32_t n, uint32_t kdim);
+
 /* Level1Kernels (zengpu-blas/src/level1.rs:51-139): in place, no allocation. */
 int zg_level1_saxpy(zg_device *dev, float alpha, const zg_device_array *x,
                     const zg_device_array *y);
@@ -315,6 +327,22 @@ int zg_sgemm_prepare(int mode, int m, int n, int k, const float *a, const float 
 int zg_sgemm_compute(int mode, int m, int n, int k, float alpha, const float *a, const float *b,
                      float *c, const float *bias, int relu, const void *workspace,
                      uint64_t workspace_bytes, void *stream);
+
+/* Packed operands, for operands reused across GEMMs (a weight matrix, or the
+ * row block of A multiplied by successive column panels of B).  A packed
+ * operand holds exactly the planes the mode's kernel reads (TF32X3: tf32
+ * hi/lo; TF32: f32; B K-major for the tensor-core modes), 256-byte aligned.
+ * pack_bytes: size for operand 0 = A (outer = m) or 1 = B (outer = n).
+ * sgemm_packed: C[m, n] (row pitch ldc >= n) = epilogue(alpha * A @ B) from
+ * packed A and B of the same mode and k. */
+uint64_t zg_sgemm_pack_bytes(int mode, int operand, int outer, int k);
+int zg_sgemm_pack_a(int mode, int m, int k, const float *a, int64_t lda, void *packed,
+                    uint64_t packed_bytes, void *stream);
+int zg_sgemm_pack_b(int mode, int k, int n, const float *b, int64_t ldb, void *packed,
+                    uint64_t packed_bytes, void *stream);
+int zg_sgemm_packed(int mode, int m, int n, int k, float alpha, const void *a_packed,
+                    const void *b_packed, float *c, int64_t ldc, const float *bias, int relu,
+                    void *stream);
 
 /* zg_sgemm_f32 for callers that cannot allocate device memory when they call
  * (no counterpart in the reference: ZenGPU's GemmKernel always allocates its

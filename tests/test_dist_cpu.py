@@ -80,3 +80,73 @@ def test_two_rank_broadcast_and_gather():
         assert p.exitcode == 0
     for rank, err in results:
         assert err < 1e-5, (rank, err)
+
+
+class _CpuOps:
+    """Stand-in for pack_a / pack_b / sgemm_packed on CPU tensors (float64
+    product): exercises the panel bookkeeping and broadcast order only."""
+
+    class P:
+        def __init__(self, t):
+            self.t = t.clone()
+            self.buf = self.t
+
+    def pack_a(self, a, mode, out=None):
+        return self.P(a)
+
+    def pack_b(self, b, mode, out=None):
+        return self.P(b)
+
+    def sgemm_packed(self, pa, pb, c, alpha=1.0, bias=None, relu=False):
+        r = alpha * (pa.t.double() @ pb.t.double())
+        if bias is not None:
+            r = r + bias.double()
+        if relu:
+            r = torch.clamp_min(r, 0.0)
+        c.copy_(r.float())
+        return c
+
+
+def _worker_pipelined(rank, world, port, m, n, k, panels, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(1)
+        a = torch.rand((m, k), generator=g) * 2 - 1
+        b_full = torch.rand((k, n), generator=g) * 2 - 1
+        bias = torch.rand(n, generator=g) - 0.5
+        b = b_full.clone() if rank == 1 else torch.zeros_like(b_full)
+        sg = ShardedGemm(mode=1, ops=_CpuOps())
+        r0, r1 = row_range(m, world, rank)
+        c = sg.sgemm_rows_pipelined(a[r0:r1].contiguous(), b, src=1, panels=panels, alpha=2.0,
+                                    bias=bias, relu=True)
+        ref = torch.clamp_min(2.0 * (a[r0:r1].double() @ b_full.double()) + bias.double(), 0)
+        q.put((rank, float((c.double() - ref).abs().max())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("panels", [1, 3, 5])
+def test_two_rank_pipelined_panels(panels):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_pipelined, args=(r, 2, port, 21, 37, 13, panels, q))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, err in results:
+        assert err < 1e-5, (rank, err)
+
+
+def test_panel_count():
+    from zengpu_b200.dist import panel_count
+    assert panel_count(8192, 8192) == 2      # 2 panels of 1024 tiles each
+    assert panel_count(4096, 32768) == 4
+    assert panel_count(1024, 8192) == 1      # too small to split
+    assert panel_count(32768, 32768) == 8

@@ -164,3 +164,111 @@ def test_gemm_api_errors(device, pool):
 
 def test_default_mode_is_tf32x3(device):
     assert zg.GemmKernel(device).mode == zg.GemmMode.TF32X3
+
+
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
+def test_packed_operands_into_column_panels(mode):
+    """pack_a once, pack_b per column panel, each GEMM written into its column
+    panel of a row-major C (pitch n) - the multi-GPU pipelined path."""
+    m, n, k = 384, 1000, 520
+    a = O.uniform(m * k, 31).reshape(m, k)
+    b = O.uniform(k * n, 32).reshape(k, n)
+    bias = O.uniform(n, 33, -0.1, 0.1)
+    ta, tb, tbias = (torch.from_numpy(x).cuda() for x in (a, b, bias))
+    pa = K.pack_a(ta, mode)
+    c = torch.full((m, n), float("nan"), device="cuda")
+    for j0, j1 in [(0, 256), (256, 600), (600, 1000)]:
+        pb = K.pack_b(tb[:, j0:j1].contiguous(), mode)
+        K.sgemm_packed(pa, pb, c[:, j0:j1], alpha=0.5, bias=tbias[j0:j1], relu=True)
+    torch.cuda.synchronize()
+    assert K.kernel_status() == 0
+    ref = O.sgemm_bias_relu(a, b, bias, alpha=0.5)
+    assert O.rel_fro(c.cpu().numpy(), ref) <= TOL[mode]
+    # packing a strided view (row pitch > k) gives the same result
+    wide = torch.zeros((m, k + 12), device="cuda")
+    wide[:, :k] = ta
+    pa2 = K.pack_a(wide[:, :k], mode)
+    c2 = K.sgemm_packed(pa2, K.pack_b(tb, mode), alpha=0.5, bias=tbias, relu=True)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(bits(c2.cpu().numpy()), bits(c.cpu().numpy()))
+
+
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
+@pytest.mark.parametrize("m,n,k", [(2500, 768, 1000), (77, 130, 65), (4096, 1024, 512)])
+def test_sgemm_host_pipelined(device, mode, m, n, k):
+    """GemmKernel.sgemm_host: host arrays in, row panels overlapped, host C out."""
+    a = O.uniform(m * k, 41).reshape(m, k)
+    b = O.uniform(k * n, 42).reshape(k, n)
+    bias = O.uniform(n, 43, -0.1, 0.1)
+    gemm = zg.GemmKernel(device, mode)
+    c = np.full((m, n), np.nan, np.float32)
+    gemm.sgemm_host(device, 1.0, a, b, c, m, n, k)
+    assert O.rel_fro(c, O.sgemm(a, b)) <= TOL[mode]
+    c2 = np.empty((m, n), np.float32)
+    gemm.sgemm_host(device, -0.25, a, b, c2, m, n, k, bias=bias, relu=True)
+    assert O.rel_fro(c2, O.sgemm_bias_relu(a, b, bias, alpha=-0.25)) <= TOL[mode]
+    # pinned torch host tensors take the same path
+    ha = torch.from_numpy(a).pin_memory()
+    hb = torch.from_numpy(b).pin_memory()
+    hc = torch.empty((m, n)).pin_memory()
+    gemm.sgemm_host(device, 1.0, ha, hb, hc, m, n, k)
+    np.testing.assert_array_equal(bits(hc.numpy()), bits(c))
+
+
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
+def test_config0_chain_gemm_add_relu(device, pool, mode):
+    """The CPU-runnable configuration end to end through the drop-in API:
+    C = A @ B (256^3, seed 0), then C + U (uniform, seed 5) and ReLU."""
+    ab = O.uniform(2 * 256 * 256, 0)
+    a, b = ab[: 256 * 256].reshape(256, 256), ab[256 * 256:].reshape(256, 256)
+    u = O.uniform(256 * 256, 5).reshape(256, 256)
+    gemm = zg.GemmKernel(device, mode)
+    ew = zg.ElementwiseKernels(device)
+    da, db, du = (zg.upload(device, pool, x) for x in (a, b, u))
+    y = ew.relu(device, pool, ew.add(device, pool, gemm.gemm(device, pool, da, db), du))
+    ref = O.relu(O.add(O.sgemm_ref(a, b), u))
+    assert O.rel_fro(zg.download(device, y), ref) <= TOL[mode]
+
+
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
+def test_8192_sampled_vs_fp64(mode):
+    """The square-sweep's largest size: 8192^3, sampled 256 x 256 blocks vs f64."""
+    n = 8192
+    ta = torch.empty((n, n), device="cuda")
+    tb = torch.empty((n, n), device="cuda")
+    K.fill_uniform(ta, 2)
+    K.fill_uniform(tb, 102)
+    c = K.sgemm(ta, tb, mode=mode)
+    torch.cuda.synchronize()
+    assert K.kernel_status() == 0
+    a, b = ta.cpu().numpy(), tb.cpu().numpy()
+    for r0, c0 in [(0, 0), (n - 256, n - 256), (3000, 5000)]:
+        ref = O.dgemm_tile(a, b, r0, c0, 256, 256)
+        assert O.rel_fro(c[r0:r0 + 256, c0:c0 + 256].cpu().numpy(), ref) <= TOL[mode]
+    del ta, tb, c
+    torch.cuda.empty_cache()
+
+
+def test_sharded_config_tiles_vs_fp64():
+    """32768 x 32768 x 8192 (seed 4) in 3xTF32, computed as two row shards the
+    way the multi-GPU path splits it; 16 random 128 x 128 tiles vs f64."""
+    m = n = 32768
+    k = 8192
+    ta = torch.empty((m, k), device="cuda")
+    tb = torch.empty((k, n), device="cuda")
+    K.fill_uniform(ta, 4)
+    K.fill_uniform(tb, 1004)
+    c = torch.empty((m, n), device="cuda")
+    for r0, r1 in [(0, m // 2), (m // 2, m)]:
+        K.sgemm(ta[r0:r1], tb, mode=zg.GemmMode.TF32X3, out=c[r0:r1])
+    torch.cuda.synchronize()
+    assert K.kernel_status() == 0
+    a, b = ta.cpu().numpy(), tb.cpu().numpy()
+    rng = np.random.default_rng(4)
+    for _ in range(16):
+        r0 = int(rng.integers(0, m // 128)) * 128
+        c0 = int(rng.integers(0, n // 128)) * 128
+        ref = O.dgemm_tile(a, b, r0, c0, 128, 128)
+        assert O.rel_fro(c[r0:r0 + 128, c0:c0 + 128].cpu().numpy(), ref) <= 1e-5
+    del ta, tb, c
+    torch.cuda.empty_cache()

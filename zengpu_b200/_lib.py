@@ -130,6 +130,8 @@ SIGNATURES: dict[str, tuple] = {
     "zg_gemm_bias_relu": (_i, [C.POINTER(CGemmKernel), _vp, _vp, _f, C.POINTER(CDeviceArray),
                                C.POINTER(CDeviceArray), C.POINTER(CDeviceArray),
                                C.POINTER(CDeviceArray)]),
+    "zg_gemm_sgemm_host": (_i, [C.POINTER(CGemmKernel), _vp, _f, _vp, _vp, _vp, _i, _vp, _u32,
+                                _u32, _u32]),
     "zg_level1_saxpy": (_i, [_vp, _f, C.POINTER(CDeviceArray), C.POINTER(CDeviceArray)]),
     "zg_level1_sscal": (_i, [_vp, _f, C.POINTER(CDeviceArray)]),
     "zg_add_f32": (_i, [_fp, _fp, _fp, _u64, _vp]),
@@ -140,6 +142,10 @@ SIGNATURES: dict[str, tuple] = {
     "zg_sgemm_f32": (_i, [_i, _i, _i, _i, _f, _fp, _fp, _fp, _fp, _i, _vp, _u64, _vp]),
     "zg_sgemm_prepare": (_i, [_i, _i, _i, _i, _fp, _fp, _vp, _u64, _vp]),
     "zg_sgemm_compute": (_i, [_i, _i, _i, _i, _f, _fp, _fp, _fp, _fp, _i, _vp, _u64, _vp]),
+    "zg_sgemm_pack_bytes": (_u64, [_i, _i, _i, _i]),
+    "zg_sgemm_pack_a": (_i, [_i, _i, _i, _fp, C.c_int64, _vp, _u64, _vp]),
+    "zg_sgemm_pack_b": (_i, [_i, _i, _i, _fp, C.c_int64, _vp, _u64, _vp]),
+    "zg_sgemm_packed": (_i, [_i, _i, _i, _i, _f, _vp, _vp, _fp, C.c_int64, _fp, _i, _vp]),
     "zg_sgemm_f32_noalloc": (_i, [_i, _i, _i, _i, _f, _fp, _fp, _fp, _fp, _i, _vp]),
     "zg_fill_uniform_f32": (_i, [_fp, _u64, _u64, _f, _f, _vp]),
     "zg_fill_normal_f32": (_i, [_fp, _u64, _u64, _vp]),

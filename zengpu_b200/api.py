@@ -435,6 +435,20 @@ class ElementwiseKernels:
         check(self._lib.zg_elementwise_relu_inplace(C.byref(self._k), device.raw, C.byref(a._c)))
 
 
+def _host_ptr(x) -> tuple[int, object]:
+    """(address, keep-alive) of a host buffer: an int address, or a C-contiguous
+    float32 numpy array (or anything exposing data_ptr(), e.g. a pinned torch
+    CPU tensor)."""
+    if x is None:
+        return 0, None
+    if isinstance(x, int):
+        return x, None
+    if hasattr(x, "data_ptr"):
+        return int(x.data_ptr()), x
+    arr = np.ascontiguousarray(x, dtype=np.float32)
+    return arr.ctypes.data, arr
+
+
 class GemmKernel:
     """f32 GEMM (zengpu-blas/src/level3.rs:101-182) with a selectable mode."""
 
@@ -480,6 +494,22 @@ class GemmKernel:
                                           C.byref(a._c), C.byref(b._c), C.byref(bias._c),
                                           C.byref(out)))
         return DeviceArray(out)
+
+
+    def sgemm_host(self, device: CudaDevice, alpha: float, a, b, c, m: int, n: int, k: int,
+                   bias=None, relu: bool = False) -> None:
+        """C = epilogue(alpha * A @ B) on host arrays (zg_gemm_sgemm_host): B up,
+        then row panels of A up / GEMM / C rows down, overlapped on three streams.
+        a, b, c, bias: host addresses, float32 numpy arrays or pinned torch tensors."""
+        pa, ka = _host_ptr(a)
+        pb, kb = _host_ptr(b)
+        pc, kc = _host_ptr(c)
+        pbias, kbias = _host_ptr(bias)
+        check(self._lib.zg_gemm_sgemm_host(C.byref(self._k), device.raw, float(alpha),
+                                           C.c_void_p(pa), C.c_void_p(pb),
+                                           C.c_void_p(pbias) if bias is not None else None,
+                                           1 if relu else 0, C.c_void_p(pc), m, n, k))
+        del ka, kb, kc, kbias
 
 
 class Level1Kernels:

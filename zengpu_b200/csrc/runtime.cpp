@@ -24,6 +24,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 #include <string>
 #include <thread>
@@ -31,6 +32,7 @@
 #include <vector>
 
 #include "zengpu_b200.h"
+#include "zg_gemm_internal.h"
 
 namespace zg {
 
@@ -264,6 +266,11 @@ struct zg_device {
     std::vector<uint32_t> deferred_buffers;  // retired slot indices
     void* workspace = nullptr;
     uint64_t workspace_bytes = 0;
+    // Pipelined host-buffer GEMM: copy streams and device staging.
+    cudaStream_t h2d = nullptr;
+    cudaStream_t d2h = nullptr;
+    void* staging = nullptr;
+    uint64_t staging_bytes = 0;
 };
 
 struct zg_submission {
@@ -530,6 +537,9 @@ extern "C" void zg_device_close(zg_device* dev) {
             if (s.module && d.ok) d.moduleUnload(s.module);
         });
         if (dev->workspace) cudaFree(dev->workspace);
+        if (dev->staging) cudaFree(dev->staging);
+        if (dev->h2d) cudaStreamDestroy(dev->h2d);
+        if (dev->d2h) cudaStreamDestroy(dev->d2h);
         cudaStreamDestroy(dev->stream);
     }
     delete dev;
@@ -1312,4 +1322,156 @@ extern "C" int zg_level1_sscal(zg_device* dev, float alpha, const zg_device_arra
     if ((rc = set_device(dev))) return rc;
     if ((rc = zg_sscal_f32(alpha, px, n, dev->stream))) return rc;
     return finish_sync(dev, false);
+}
+
+// ======================================================================
+// Pipelined GEMM on host arrays
+// ======================================================================
+
+namespace zg {
+namespace {
+
+uint64_t align256(uint64_t x) { return (x + 255) / 256 * 256; }
+
+int ensure_staging(zg_device* dev, uint64_t bytes) {
+    if (bytes <= dev->staging_bytes) return ZG_OK;
+    if (dev->staging) {
+        cudaDeviceSynchronize();
+        cudaFree(dev->staging);
+        dev->staging = nullptr;
+        dev->staging_bytes = 0;
+    }
+    int rc = cuda_status(cudaMalloc(&dev->staging, bytes), "host-gemm staging alloc");
+    if (rc == ZG_OK) dev->staging_bytes = bytes;
+    return rc;
+}
+
+int ensure_copy_streams(zg_device* dev) {
+    int rc = ZG_OK;
+    if (!dev->h2d)
+        rc = cuda_status(cudaStreamCreateWithFlags(&dev->h2d, cudaStreamNonBlocking), "h2d stream");
+    if (!rc && !dev->d2h)
+        rc = cuda_status(cudaStreamCreateWithFlags(&dev->d2h, cudaStreamNonBlocking), "d2h stream");
+    return rc;
+}
+
+}  // namespace
+}  // namespace zg
+
+extern "C" int zg_gemm_sgemm_host(const zg_gemm_kernel* kern, zg_device* dev, float alpha,
+                                  const float* a, const float* b, const float* bias, int relu,
+                                  float* c, uint32_t m, uint32_t n, uint32_t k) {
+    if (!kern || !dev) return set_error(ZG_ERR_DISPATCH, "sgemm_host: null kernel or device");
+    if (m > 0x7fffffffu || n > 0x7fffffffu || k > 0x7fffffffu)
+        return set_error(ZG_ERR_DISPATCH, "sgemm_host: dimension exceeds 2^31-1");
+    if (m == 0 || n == 0) return ZG_OK;
+    if (!c || (k > 0 && (!a || !b))) return set_error(ZG_ERR_DISPATCH, "sgemm_host: null host pointer");
+    const int mode = kern->mode;
+    if (mode != ZG_GEMM_SIMT_FP32 && mode != ZG_GEMM_TF32X3 && mode != ZG_GEMM_TF32)
+        return set_error(ZG_ERR_DISPATCH, "sgemm: unknown mode %d", mode);
+    std::lock_guard<std::recursive_mutex> lk(dev->mu);
+    int rc = set_device(dev);
+    if (rc) return rc;
+    if (in_flight(dev))
+        return set_error(ZG_ERR_BINDING_MISMATCH,
+                         "sgemm_host cannot run while an asynchronous submission is pending");
+    if ((rc = ensure_copy_streams(dev))) return rc;
+    const int M = static_cast<int>(m), N = static_cast<int>(n), K = static_cast<int>(k);
+    const int64_t kp = gemm_plane_pitch(K);
+    const bool a_planes = K > 0 && gemm_a_needs_planes(mode, K);
+    const bool b_planes = K > 0 && gemm_b_needs_planes(mode);
+    const bool lo = mode == ZG_GEMM_TF32X3;
+    // Staging layout: A, B, C, bias, A planes (hi, lo), B^T planes (hi, lo).
+    uint64_t off = 0;
+    const uint64_t o_a = off; off += align256(uint64_t(M) * K * 4);
+    const uint64_t o_b = off; off += align256(uint64_t(K) * N * 4);
+    const uint64_t o_c = off; off += align256(uint64_t(M) * N * 4);
+    const uint64_t o_bias = off; off += align256(uint64_t(N) * 4);
+    const uint64_t o_ah = off; off += a_planes ? align256(uint64_t(M) * kp * 4) : 0;
+    const uint64_t o_al = off; off += a_planes && lo ? align256(uint64_t(M) * kp * 4) : 0;
+    const uint64_t o_bh = off; off += b_planes ? align256(uint64_t(N) * kp * 4) : 0;
+    const uint64_t o_bl = off; off += b_planes && lo ? align256(uint64_t(N) * kp * 4) : 0;
+    if ((rc = ensure_staging(dev, off))) return rc;
+    uint8_t* base = static_cast<uint8_t*>(dev->staging);
+    float* dA = reinterpret_cast<float*>(base + o_a);
+    float* dB = reinterpret_cast<float*>(base + o_b);
+    float* dC = reinterpret_cast<float*>(base + o_c);
+    float* dBias = reinterpret_cast<float*>(base + o_bias);
+    float* ah = reinterpret_cast<float*>(base + o_ah);
+    float* al = lo ? reinterpret_cast<float*>(base + o_al) : nullptr;
+    float* bh = reinterpret_cast<float*>(base + o_bh);
+    float* bl = lo ? reinterpret_cast<float*>(base + o_bl) : nullptr;
+
+    // Row panels of A / C: large enough to keep the GEMM efficient, small
+    // enough that uploading A, computing and downloading C overlap.
+    const int rows = M <= 1024 ? M : std::max(512, (((M + 7) / 8 + 127) / 128) * 128);
+    const int panels = (M + rows - 1) / rows;
+    std::vector<cudaEvent_t> ev(2 * panels + 1, nullptr);
+    for (auto& e : ev)
+        if ((rc = cuda_status(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event")))
+            break;
+    cudaStream_t comp = dev->stream;
+    if (!rc && K > 0) rc = cuda_status(cudaMemcpyAsync(dB, b, uint64_t(K) * N * 4,
+                                                       cudaMemcpyHostToDevice, dev->h2d), "H2D B");
+    if (!rc && bias)
+        rc = cuda_status(cudaMemcpyAsync(dBias, bias, uint64_t(N) * 4, cudaMemcpyHostToDevice,
+                                         dev->h2d), "H2D bias");
+    if (!rc) rc = cuda_status(cudaEventRecord(ev[0], dev->h2d), "event");
+    for (int p = 0; p < panels && !rc; ++p) {
+        const int r0 = p * rows, nr = std::min(rows, M - r0);
+        if (K > 0)
+            rc = cuda_status(cudaMemcpyAsync(dA + int64_t(r0) * K, a + int64_t(r0) * K,
+                                             uint64_t(nr) * K * 4, cudaMemcpyHostToDevice, dev->h2d),
+                             "H2D A panel");
+        if (!rc) rc = cuda_status(cudaEventRecord(ev[1 + p], dev->h2d), "event");
+    }
+    if (!rc) rc = cuda_status(cudaStreamWaitEvent(comp, ev[0], 0), "wait B");
+    if (!rc && b_planes) rc = gemm_prep_b(mode, K, N, dB, N, bh, bl, kp, comp);
+    for (int p = 0; p < panels && !rc; ++p) {
+        const int r0 = p * rows, nr = std::min(rows, M - r0);
+        if ((rc = cuda_status(cudaStreamWaitEvent(comp, ev[1 + p], 0), "wait A panel"))) break;
+        float* cp = dC + int64_t(r0) * N;
+        if (K == 0) {
+            rc = zg_sgemm_f32(mode, nr, N, 0, alpha, nullptr, nullptr, cp, bias ? dBias : nullptr,
+                              relu, nullptr, 0, comp);
+        } else {
+            const float* ap = dA + int64_t(r0) * K;
+            if (a_planes &&
+                (rc = gemm_prep_a(mode, nr, K, ap, K, ah + int64_t(r0) * kp,
+                                  lo ? al + int64_t(r0) * kp : nullptr, kp, comp)))
+                break;
+            GemmOperands op{mode, ap, nullptr, K, dB, nullptr, N};
+            if (a_planes) {
+                op.a_hi = ah + int64_t(r0) * kp;
+                op.a_lo = lo ? al + int64_t(r0) * kp : nullptr;
+                op.lda = kp;
+            }
+            if (b_planes) {
+                op.b_hi = bh;
+                op.b_lo = bl;
+                op.ldb = kp;
+            }
+            rc = gemm_run(op, nr, N, K, alpha, cp, N, bias ? dBias : nullptr, relu, comp);
+        }
+        if (!rc) rc = cuda_status(cudaEventRecord(ev[1 + panels + p], comp), "event");
+        if (!rc) rc = cuda_status(cudaStreamWaitEvent(dev->d2h, ev[1 + panels + p], 0), "wait C");
+        if (!rc)
+            rc = cuda_status(cudaMemcpyAsync(c + int64_t(r0) * N, cp, uint64_t(nr) * N * 4,
+                                             cudaMemcpyDeviceToHost, dev->d2h),
+                             "D2H C panel");
+    }
+    // Drain all three streams whatever happened, then report.
+    cudaStreamSynchronize(dev->h2d);
+    cudaStreamSynchronize(comp);
+    const int sync_rc = cuda_status(cudaStreamSynchronize(dev->d2h), "sgemm_host sync");
+    for (auto& e : ev)
+        if (e) cudaEventDestroy(e);
+    if (rc) return rc;
+    if (sync_rc) return sync_rc;
+    uint32_t code = 0;
+    if ((rc = zg_kernel_status(&code))) return rc;
+    if (code)
+        return set_error(ZG_ERR_KERNEL_WAIT,
+                         "kernel bounded wait expired (status 0x%x); results are invalid", code);
+    return ZG_OK;
 }

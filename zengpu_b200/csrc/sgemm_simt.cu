@@ -22,9 +22,9 @@ constexpr int kPadA = 4;  // As row pitch 132 floats: 16-byte aligned rows
 
 template <bool kVecA, bool kVecB>
 __global__ void __launch_bounds__(kThreads, 2)
-    sgemm_simt_kernel(int M, int N, int K, float alpha, const float* __restrict__ A,
-                      const float* __restrict__ B, float* __restrict__ C,
-                      const float* __restrict__ bias, int relu, int vec_c) {
+    sgemm_simt_kernel(int M, int N, int K, float alpha, const float* __restrict__ A, int64_t lda,
+                      const float* __restrict__ B, int64_t ldb, float* __restrict__ C,
+                      int64_t ldc, const float* __restrict__ bias, int relu, int vec_c) {
     __shared__ __align__(16) float As[2][BK][BM + kPadA];
     __shared__ __align__(16) float Bs[2][BK][BN];
 
@@ -45,26 +45,26 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int kk = k0 + a_kq;
             if (kVecA) {
                 ra[j] = (row < M && kk < K)
-                            ? __ldg(reinterpret_cast<const float4*>(A + (size_t)row * K + kk))
+                            ? __ldg(reinterpret_cast<const float4*>(A + row * lda + kk))
                             : make_float4(0.f, 0.f, 0.f, 0.f);
             } else {
                 float v[4];
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
-                    v[c] = (row < M && kk + c < K) ? __ldg(A + (size_t)row * K + kk + c) : 0.f;
+                    v[c] = (row < M && kk + c < K) ? __ldg(A + row * lda + kk + c) : 0.f;
                 ra[j] = make_float4(v[0], v[1], v[2], v[3]);
             }
             const int krow = k0 + b_k + 8 * j;
             const int col = n0 + b_nq;
             if (kVecB) {
                 rb[j] = (krow < K && col < N)
-                            ? __ldg(reinterpret_cast<const float4*>(B + (size_t)krow * N + col))
+                            ? __ldg(reinterpret_cast<const float4*>(B + krow * ldb + col))
                             : make_float4(0.f, 0.f, 0.f, 0.f);
             } else {
                 float v[4];
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
-                    v[c] = (krow < K && col + c < N) ? __ldg(B + (size_t)krow * N + col + c) : 0.f;
+                    v[c] = (krow < K && col + c < N) ? __ldg(B + krow * ldb + col + c) : 0.f;
                 rb[j] = make_float4(v[0], v[1], v[2], v[3]);
             }
         }
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 if (relu) x = relu1(x);
                 v[c] = x;
             }
-            float* dst = C + (size_t)row * N + col;
+            float* dst = C + row * ldc + col;
             if (vec_c && col + 3 < N) {
                 *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
             } else {
@@ -144,24 +144,25 @@ __global__ void __launch_bounds__(kThreads, 2)
 }  // namespace
 
 // Launches the SIMT SGEMM on `stream`; shapes already validated by the caller.
-int launch_sgemm_simt(int M, int N, int K, float alpha, const float* A, const float* B, float* C,
-                      const float* bias, int relu, cudaStream_t stream) {
-    const bool va = (K % 4 == 0) && ((reinterpret_cast<uintptr_t>(A) & 15u) == 0);
-    const bool vb = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(B) & 15u) == 0);
-    const int vc = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
+int launch_sgemm_simt(int M, int N, int K, float alpha, const float* A, int64_t lda,
+                      const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias,
+                      int relu, cudaStream_t stream) {
+    const bool va = (lda % 4 == 0) && ((reinterpret_cast<uintptr_t>(A) & 15u) == 0);
+    const bool vb = (ldb % 4 == 0) && ((reinterpret_cast<uintptr_t>(B) & 15u) == 0);
+    const int vc = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
     if (va && vb)
-        sgemm_simt_kernel<true, true><<<grid, kThreads, 0, stream>>>(M, N, K, alpha, A, B, C, bias,
-                                                                     relu, vc);
+        sgemm_simt_kernel<true, true><<<grid, kThreads, 0, stream>>>(M, N, K, alpha, A, lda, B, ldb, C, ldc,
+                                                                     bias, relu, vc);
     else if (va)
-        sgemm_simt_kernel<true, false><<<grid, kThreads, 0, stream>>>(M, N, K, alpha, A, B, C,
-                                                                      bias, relu, vc);
+        sgemm_simt_kernel<true, false><<<grid, kThreads, 0, stream>>>(M, N, K, alpha, A, lda, B, ldb, C,
+                                                                      ldc, bias, relu, vc);
     else if (vb)
-        sgemm_simt_kernel<false, true><<<grid, kThreads, 0, stream>>>(M, N, K, alpha, A, B, C,
-                                                                      bias, relu, vc);
+        sgemm_simt_kernel<false, true><<<grid, kThreads, 0, stream>>>(M, N, K, alpha, A, lda, B, ldb, C,
+                                                                      ldc, bias, relu, vc);
     else
-        sgemm_simt_kernel<false, false><<<grid, kThreads, 0, stream>>>(M, N, K, alpha, A, B, C,
-                                                                       bias, relu, vc);
+        sgemm_simt_kernel<false, false><<<grid, kThreads, 0, stream>>>(M, N, K, alpha, A, lda, B, ldb, C,
+                                                                       ldc, bias, relu, vc);
     return cuda_status(cudaGetLastError(), "sgemm_simt");
 }
 

@@ -34,13 +34,15 @@
 #include <mutex>
 
 #include "zg_common.cuh"
+#include "zg_gemm_internal.h"
 
 namespace zg {
 
 __device__ uint32_t g_status = 0;
 
-int launch_sgemm_simt(int M, int N, int K, float alpha, const float* A, const float* B, float* C,
-                      const float* bias, int relu, cudaStream_t stream);
+int launch_sgemm_simt(int M, int N, int K, float alpha, const float* A, int64_t lda,
+                      const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias,
+                      int relu, cudaStream_t stream);
 
 namespace {
 
@@ -104,7 +106,8 @@ __device__ __forceinline__ void tile_coords(int tile, int mt, int nt, int& m_til
 template <int kPlanes>
 __global__ void __launch_bounds__(kTcThreads, 1)
     sgemm_tc_kernel(const __grid_constant__ TcMaps maps, int M, int N, int K, float alpha,
-                    float* __restrict__ C, const float* __restrict__ bias, int relu, int vec_c) {
+                    float* __restrict__ C, int64_t ldc, const float* __restrict__ bias, int relu,
+                    int vec_c) {
     using Cfg = TcCfg<kPlanes>;
     constexpr int BK = Cfg::BK, STAGES = Cfg::STAGES;
 
@@ -270,7 +273,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         if (relu) x = relu1(x);
                         v[t] = x;
                     }
-                    float* dst = C + static_cast<size_t>(row) * N + col0;
+                    float* dst = C + static_cast<int64_t>(row) * ldc + col0;
                     if (vec_c && col0 + 32 <= N) {
 #pragma unroll
                         for (int t = 0; t < 32; t += 4)
@@ -473,8 +476,8 @@ int launch_transpose(const float* src, int K, int N, int64_t lds, float* hi, flo
 }
 
 template <int kPlanes>
-int launch_tc(const TcMaps& maps, int M, int N, int K, float alpha, float* C, const float* bias,
-              int relu, cudaStream_t s) {
+int launch_tc(const TcMaps& maps, int M, int N, int K, float alpha, float* C, int64_t ldc,
+              const float* bias, int relu, cudaStream_t s) {
     using Cfg = TcCfg<kPlanes>;
     static std::once_flag attr_once;
     static cudaError_t attr_err = cudaSuccess;
@@ -485,68 +488,105 @@ int launch_tc(const TcMaps& maps, int M, int N, int K, float alpha, float* C, co
     });
     if (attr_err != cudaSuccess) return cuda_status(attr_err, "sgemm_tc smem attribute");
     const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
-    const int vec_c = (N % 4 == 0) && aligned16(C);
+    const int vec_c = (ldc % 4 == 0) && aligned16(C);
     sgemm_tc_kernel<kPlanes><<<mt * nt, kTcThreads, Cfg::SMEM_BYTES, s>>>(maps, M, N, K, alpha, C,
-                                                                         bias, relu, vec_c);
+                                                                         ldc, bias, relu, vec_c);
     return cuda_status(cudaGetLastError(), "sgemm_tc");
 }
 
-// Writes the planes the tensor-core kernel reads: tf32 hi/lo of A and B
-// (TF32X3), or pitch-padded copies (TF32 with k or n not a multiple of 4).
-int prepare_planes(int mode, int M, int N, int K, const float* A, const float* B, uint8_t* ws,
-                   cudaStream_t s) {
-    const WsLayout w = ws_layout(mode, M, N, K);
-    const int64_t kp = static_cast<int64_t>(round_up(K, 4));
-    int rc = ZG_OK;
-    if (mode == ZG_GEMM_TF32X3) {
-        if ((rc = launch_split(A, M, K, K, reinterpret_cast<float*>(ws + w.a_hi),
-                               reinterpret_cast<float*>(ws + w.a_lo), kp, 1, s)) != ZG_OK)
-            return rc;
-        return launch_transpose(B, K, N, N, reinterpret_cast<float*>(ws + w.b_hi),
-                                reinterpret_cast<float*>(ws + w.b_lo), kp, 1, s);
-    }
-    if (mode == ZG_GEMM_TF32) {
-        if (w.a_hi != kNone &&
-            (rc = launch_split(A, M, K, K, reinterpret_cast<float*>(ws + w.a_hi), nullptr, kp, 0,
-                               s)) != ZG_OK)
-            return rc;
-        rc = launch_transpose(B, K, N, N, reinterpret_cast<float*>(ws + w.b_hi), nullptr, kp, 0, s);
-    }
-    return rc;
+}  // namespace
+
+// ---- GEMM building blocks (shared with the runtime's pipelined host GEMM) ----
+bool gemm_a_needs_planes(int mode, int K) {
+    return mode == ZG_GEMM_TF32X3 || (mode == ZG_GEMM_TF32 && K % 4 != 0);
+}
+bool gemm_b_needs_planes(int mode) { return mode == ZG_GEMM_TF32X3 || mode == ZG_GEMM_TF32; }
+int64_t gemm_plane_pitch(int K) { return static_cast<int64_t>(round_up(K, 4)); }
+
+int gemm_prep_a(int mode, int M, int K, const float* A, int64_t lda, float* hi, float* lo,
+                int64_t ldp, cudaStream_t s) {
+    if (mode == ZG_GEMM_TF32X3) return launch_split(A, M, K, lda, hi, lo, ldp, 1, s);
+    if (mode == ZG_GEMM_TF32 && K % 4 != 0)
+        return launch_split(A, M, K, lda, hi, nullptr, ldp, 0, s);
+    return ZG_OK;
 }
 
-// Encodes the tensor maps over the prepared planes (or the raw operands) and
-// launches the tcgen05 kernel.
-int compute_planes(int mode, int M, int N, int K, float alpha, const float* A, const float* B,
-                   float* C, const float* bias, int relu, const uint8_t* ws, cudaStream_t s) {
-    (void)B;
-    const WsLayout w = ws_layout(mode, M, N, K);
-    const int64_t kp = static_cast<int64_t>(round_up(K, 4));
+int gemm_prep_b(int mode, int K, int N, const float* B, int64_t ldb, float* hi, float* lo,
+                int64_t ldp, cudaStream_t s) {
+    if (mode == ZG_GEMM_TF32X3) return launch_transpose(B, K, N, ldb, hi, lo, ldp, 1, s);
+    if (mode == ZG_GEMM_TF32) return launch_transpose(B, K, N, ldb, hi, nullptr, ldp, 0, s);
+    return ZG_OK;
+}
+
+int gemm_run(const GemmOperands& op, int M, int N, int K, float alpha, float* C, int64_t ldc,
+             const float* bias, int relu, cudaStream_t s) {
+    if (op.mode == ZG_GEMM_SIMT_FP32)
+        return launch_sgemm_simt(M, N, K, alpha, op.a_hi, op.lda, op.b_hi, op.ldb, C, ldc, bias,
+                                 relu, s);
     TcMaps maps;
     std::memset(&maps, 0, sizeof(maps));
     int rc;
-    auto plane = [&](uint64_t off) { return reinterpret_cast<const float*>(ws + off); };
-    if (mode == ZG_GEMM_TF32X3) {
+    if (!aligned16(op.a_hi) || !aligned16(op.b_hi) || op.lda % 4 != 0 || op.ldb % 4 != 0)
+        return set_error(ZG_ERR_DISPATCH,
+                         "sgemm (tensor-core mode): operand planes must be 16-byte aligned with a "
+                         "pitch that is a multiple of 4 floats");
+    if (op.mode == ZG_GEMM_TF32X3) {
         using Cfg = TcCfg<2>;
         const CUtensorMapSwizzle swz =
             Cfg::BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-        if ((rc = encode_map(&maps.a[0], plane(w.a_hi), K, M, kp, Cfg::BK, BM, swz))) return rc;
-        if ((rc = encode_map(&maps.a[1], plane(w.a_lo), K, M, kp, Cfg::BK, BM, swz))) return rc;
-        if ((rc = encode_map(&maps.b[0], plane(w.b_hi), K, N, kp, Cfg::BK, BN, swz))) return rc;
-        if ((rc = encode_map(&maps.b[1], plane(w.b_lo), K, N, kp, Cfg::BK, BN, swz))) return rc;
-        return launch_tc<2>(maps, M, N, K, alpha, C, bias, relu, s);
+        if ((rc = encode_map(&maps.a[0], op.a_hi, K, M, op.lda, Cfg::BK, BM, swz))) return rc;
+        if ((rc = encode_map(&maps.a[1], op.a_lo, K, M, op.lda, Cfg::BK, BM, swz))) return rc;
+        if ((rc = encode_map(&maps.b[0], op.b_hi, K, N, op.ldb, Cfg::BK, BN, swz))) return rc;
+        if ((rc = encode_map(&maps.b[1], op.b_lo, K, N, op.ldb, Cfg::BK, BN, swz))) return rc;
+        return launch_tc<2>(maps, M, N, K, alpha, C, ldc, bias, relu, s);
     }
     using Cfg = TcCfg<1>;
-    const float* a_src = w.a_hi != kNone ? plane(w.a_hi) : A;
-    const int64_t lda = w.a_hi != kNone ? kp : K;
-    if (!aligned16(a_src))
-        return set_error(ZG_ERR_DISPATCH, "sgemm (TF32 mode): A must start on a 16-byte boundary");
-    if ((rc = encode_map(&maps.a[0], a_src, K, M, lda, Cfg::BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
-        return rc;
-    if ((rc = encode_map(&maps.b[0], plane(w.b_hi), K, N, kp, Cfg::BK, BN,
+    if ((rc = encode_map(&maps.a[0], op.a_hi, K, M, op.lda, Cfg::BK, BM,
                          CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
-    return launch_tc<1>(maps, M, N, K, alpha, C, bias, relu, s);
+    if ((rc = encode_map(&maps.b[0], op.b_hi, K, N, op.ldb, Cfg::BK, BN,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
+        return rc;
+    return launch_tc<1>(maps, M, N, K, alpha, C, ldc, bias, relu, s);
+}
+
+namespace {
+
+// The operands zg_sgemm_compute reads for (mode, m, n, k) in workspace `ws`.
+GemmOperands operands_in_workspace(int mode, int M, int N, int K, const float* A,
+                                   const float* B, const uint8_t* ws) {
+    const WsLayout w = ws_layout(mode, M, N, K);
+    const int64_t kp = gemm_plane_pitch(K);
+    auto plane = [&](uint64_t off) {
+        return off == kNone ? nullptr : reinterpret_cast<const float*>(ws + off);
+    };
+    GemmOperands op{mode, A, nullptr, K, B, nullptr, N};
+    if (mode == ZG_GEMM_SIMT_FP32) return op;
+    if (w.a_hi != kNone) {
+        op.a_hi = plane(w.a_hi);
+        op.a_lo = plane(w.a_lo);
+        op.lda = kp;
+    }
+    op.b_hi = plane(w.b_hi);
+    op.b_lo = plane(w.b_lo);
+    op.ldb = kp;
+    return op;
+}
+
+int prepare_planes(int mode, int M, int N, int K, const float* A, const float* B, uint8_t* ws,
+                   cudaStream_t s) {
+    const WsLayout w = ws_layout(mode, M, N, K);
+    const int64_t kp = gemm_plane_pitch(K);
+    auto plane = [&](uint64_t off) {
+        return off == kNone ? nullptr : reinterpret_cast<float*>(ws + off);
+    };
+    int rc = ZG_OK;
+    if (gemm_a_needs_planes(mode, K) &&
+        (rc = gemm_prep_a(mode, M, K, A, K, plane(w.a_hi), plane(w.a_lo), kp, s)) != ZG_OK)
+        return rc;
+    if (gemm_b_needs_planes(mode))
+        rc = gemm_prep_b(mode, K, N, B, N, plane(w.b_hi), plane(w.b_lo), kp, s);
+    return rc;
 }
 
 // Shared argument checks of the three GEMM entry points.  Returns ZG_OK and
@@ -606,9 +646,9 @@ extern "C" int zg_sgemm_compute(int mode, int m, int n, int k, float alpha, cons
         gemm_k0_kernel<<<split_grid(m), 256, 0, s>>>(m, n, alpha, c, bias, relu);
         return cuda_status(cudaGetLastError(), "sgemm k=0");
     }
-    if (mode == ZG_GEMM_SIMT_FP32) return launch_sgemm_simt(m, n, k, alpha, a, b, c, bias, relu, s);
-    return compute_planes(mode, m, n, k, alpha, a, b, c, bias, relu,
-                          static_cast<const uint8_t*>(workspace), s);
+    const GemmOperands op =
+        operands_in_workspace(mode, m, n, k, a, b, static_cast<const uint8_t*>(workspace));
+    return gemm_run(op, m, n, k, alpha, c, n, bias, relu, s);
 }
 
 extern "C" int zg_sgemm_f32(int mode, int m, int n, int k, float alpha, const float* a,
@@ -618,6 +658,99 @@ extern "C" int zg_sgemm_f32(int mode, int m, int n, int k, float alpha, const fl
     if (rc) return rc;
     return zg_sgemm_compute(mode, m, n, k, alpha, a, b, c, bias, relu, workspace,
                             workspace_bytes, stream);
+}
+
+// ---- packed operands ----------------------------------------------------------
+// A packed operand is the plane(s) the GEMM kernel of `mode` reads, each
+// 256-byte aligned, row pitch kp = k rounded up to 4 floats:
+//   A (m x k):  TF32X3 hi, lo;  TF32 one f32 copy;  SIMT one f32 copy.
+//   B (k x n):  TF32X3 B^T hi, lo (n x kp, K-major);  TF32 B^T;  SIMT B itself
+//               (k rows, pitch round_up(n, 4)).
+namespace zg {
+namespace {
+uint64_t packed_plane_bytes(int mode, int operand, int outer, int k) {
+    if (mode == ZG_GEMM_SIMT_FP32 && operand == 1)
+        return round_up(static_cast<uint64_t>(k) * round_up(outer, 4) * 4, 256);
+    return round_up(static_cast<uint64_t>(outer) * round_up(k, 4) * 4, 256);
+}
+int packed_planes(int mode) { return mode == ZG_GEMM_TF32X3 ? 2 : 1; }
+bool valid_mode(int mode) {
+    return mode == ZG_GEMM_SIMT_FP32 || mode == ZG_GEMM_TF32X3 || mode == ZG_GEMM_TF32;
+}
+}  // namespace
+}  // namespace zg
+
+extern "C" uint64_t zg_sgemm_pack_bytes(int mode, int operand, int outer, int k) {
+    if (!valid_mode(mode) || (operand != 0 && operand != 1) || outer <= 0 || k <= 0) return 0;
+    return packed_planes(mode) * packed_plane_bytes(mode, operand, outer, k);
+}
+
+extern "C" int zg_sgemm_pack_a(int mode, int m, int k, const float* a, int64_t lda, void* packed,
+                               uint64_t packed_bytes, void* stream) {
+    if (!valid_mode(mode)) return set_error(ZG_ERR_DISPATCH, "sgemm pack: unknown mode %d", mode);
+    if (m < 0 || k < 0 || lda < k) return set_error(ZG_ERR_DISPATCH, "sgemm pack_a: bad shape");
+    if (m == 0 || k == 0) return ZG_OK;
+    const uint64_t need = zg_sgemm_pack_bytes(mode, 0, m, k);
+    if (!a || !packed || packed_bytes < need || (reinterpret_cast<uintptr_t>(packed) & 255u))
+        return set_error(ZG_ERR_DISPATCH,
+                         "sgemm pack_a: needs a 256-byte aligned buffer of %llu bytes",
+                         (unsigned long long)need);
+    float* hi = static_cast<float*>(packed);
+    float* lo = mode == ZG_GEMM_TF32X3
+                    ? reinterpret_cast<float*>(static_cast<uint8_t*>(packed) +
+                                               packed_plane_bytes(mode, 0, m, k))
+                    : nullptr;
+    return launch_split(a, m, k, lda, hi, lo, gemm_plane_pitch(k), mode == ZG_GEMM_TF32X3 ? 1 : 0,
+                        static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int zg_sgemm_pack_b(int mode, int k, int n, const float* b, int64_t ldb, void* packed,
+                               uint64_t packed_bytes, void* stream) {
+    if (!valid_mode(mode)) return set_error(ZG_ERR_DISPATCH, "sgemm pack: unknown mode %d", mode);
+    if (n < 0 || k < 0 || ldb < n) return set_error(ZG_ERR_DISPATCH, "sgemm pack_b: bad shape");
+    if (n == 0 || k == 0) return ZG_OK;
+    const uint64_t need = zg_sgemm_pack_bytes(mode, 1, n, k);
+    if (!b || !packed || packed_bytes < need || (reinterpret_cast<uintptr_t>(packed) & 255u))
+        return set_error(ZG_ERR_DISPATCH,
+                         "sgemm pack_b: needs a 256-byte aligned buffer of %llu bytes",
+                         (unsigned long long)need);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* hi = static_cast<float*>(packed);
+    if (mode == ZG_GEMM_SIMT_FP32)
+        return launch_split(b, k, n, ldb, hi, nullptr, static_cast<int64_t>(round_up(n, 4)), 0, s);
+    float* lo = mode == ZG_GEMM_TF32X3
+                    ? reinterpret_cast<float*>(static_cast<uint8_t*>(packed) +
+                                               packed_plane_bytes(mode, 1, n, k))
+                    : nullptr;
+    return gemm_prep_b(mode, k, n, b, ldb, hi, lo, gemm_plane_pitch(k), s);
+}
+
+extern "C" int zg_sgemm_packed(int mode, int m, int n, int k, float alpha, const void* a_packed,
+                               const void* b_packed, float* c, int64_t ldc, const float* bias,
+                               int relu, void* stream) {
+    if (!valid_mode(mode)) return set_error(ZG_ERR_DISPATCH, "sgemm: unknown mode %d", mode);
+    if (m < 0 || n < 0 || k < 0 || ldc < n)
+        return set_error(ZG_ERR_DISPATCH, "sgemm_packed: bad shape %d x %d x %d, ldc %lld", m, n,
+                         k, (long long)ldc);
+    if (m == 0 || n == 0) return ZG_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (!c) return set_error(ZG_ERR_DISPATCH, "sgemm_packed: null C");
+    if (k == 0) {
+        if (ldc != n) return set_error(ZG_ERR_DISPATCH, "sgemm_packed: k = 0 needs ldc = n");
+        gemm_k0_kernel<<<split_grid(m), 256, 0, s>>>(m, n, alpha, c, bias, relu);
+        return cuda_status(cudaGetLastError(), "sgemm k=0");
+    }
+    if (!a_packed || !b_packed) return set_error(ZG_ERR_DISPATCH, "sgemm_packed: null operand");
+    const uint8_t* pa = static_cast<const uint8_t*>(a_packed);
+    const uint8_t* pb = static_cast<const uint8_t*>(b_packed);
+    GemmOperands op{mode, reinterpret_cast<const float*>(pa), nullptr, gemm_plane_pitch(k),
+                    reinterpret_cast<const float*>(pb), nullptr, gemm_plane_pitch(k)};
+    if (mode == ZG_GEMM_TF32X3) {
+        op.a_lo = reinterpret_cast<const float*>(pa + packed_plane_bytes(mode, 0, m, k));
+        op.b_lo = reinterpret_cast<const float*>(pb + packed_plane_bytes(mode, 1, n, k));
+    }
+    if (mode == ZG_GEMM_SIMT_FP32) op.ldb = static_cast<int64_t>(round_up(n, 4));
+    return gemm_run(op, m, n, k, alpha, c, ldc, bias, relu, s);
 }
 
 extern "C" int zg_kernel_status(uint32_t* code) {

@@ -40,6 +40,20 @@ def chunk_range(n: int, world: int, rank: int, align: int = 4) -> tuple[int, int
     return min(u0 * align, n), min(u1 * align, n)
 
 
+def panel_count(m: int, n: int, tile_m: int = 128, tile_n: int = 256,
+                min_tiles: int = 900, max_panels: int = 8) -> int:
+    """Column panels for the pipelined broadcast: as many as possible (up to
+    max_panels) while each panel's GEMM still fills the GPU with at least
+    min_tiles output tiles (about six waves of 148 SMs)."""
+    tiles_m = (m + tile_m - 1) // tile_m
+    best = 1
+    for p in range(1, max_panels + 1):
+        w = (n + p - 1) // p
+        if tiles_m * ((w + tile_n - 1) // tile_n) >= min_tiles:
+            best = p
+    return best
+
+
 def _default_compute(a, b, alpha, bias, relu, mode, out):
     from . import kernels
     return kernels.sgemm(a, b, mode=mode, alpha=alpha, bias=bias, relu=relu, out=out)
@@ -49,12 +63,16 @@ class ShardedGemm:
     """C[row0:row1] = epilogue(alpha * A[row0:row1] @ B) on every rank."""
 
     def __init__(self, group=None, mode: int = 1,
-                 compute: Callable | None = None):
+                 compute: Callable | None = None, ops=None):
+        """compute: per-shard GEMM for sgemm_rows (default: the library's).
+        ops: object with pack_a / pack_b / sgemm_packed for the pipelined path
+        (default: zengpu_b200.kernels); the CPU tests pass a stand-in."""
         self.group = group
         self.mode = mode
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.compute = compute or _default_compute
+        self.ops = ops
 
     def broadcast_b(self, b: torch.Tensor, src: int = 0) -> torch.Tensor:
         """Broadcasts B (same shape and dtype on every rank) from `src`."""
@@ -70,6 +88,64 @@ class ShardedGemm:
         if broadcast:
             self.broadcast_b(b, src)
         return self.compute(a_rows, b, alpha, bias, relu, self.mode, out)
+
+    def sgemm_rows_pipelined(self, a_rows: torch.Tensor, b: torch.Tensor, src: int = 0,
+                             panels: int | None = None, alpha: float = 1.0,
+                             bias: torch.Tensor | None = None, relu: bool = False,
+                             out: torch.Tensor | None = None) -> torch.Tensor:
+        """C[row0:row1] = epilogue(alpha * A[row0:row1] @ B) with B broadcast in
+        column panels: the broadcast of panel j+1 runs on NCCL's stream while
+        panel j is multiplied, so only the first panel's transfer is exposed.
+
+        B must have its full shape on every rank (contents only on `src`).  A is
+        packed once; each panel of B is packed as it arrives and multiplied
+        into its column panel of C (row pitch n)."""
+        if self.ops is None:
+            from . import kernels as K
+        else:
+            K = self.ops
+
+        k, n = b.shape
+        m = a_rows.shape[0]
+        if a_rows.dim() != 2 or a_rows.shape[1] != k:
+            raise ValueError(f"bad shapes {tuple(a_rows.shape)} @ {tuple(b.shape)}")
+        if panels is None:
+            panels = panel_count(m, n)
+        widths = [row_range(n, panels, j) for j in range(panels)]
+        c = out if out is not None else torch.empty((m, n), dtype=torch.float32,
+                                                    device=a_rows.device)
+        # NCCL moves contiguous buffers: with one panel B itself is broadcast in
+        # place; otherwise each column panel gets its own staging buffer
+        # (together the size of B), so no panel waits for another's reuse.
+        if panels == 1 and b.is_contiguous():
+            bufs = [b]
+        else:
+            bufs = [torch.empty((k, j1 - j0), dtype=b.dtype, device=b.device)
+                    for j0, j1 in widths]
+        packed_b = None
+
+        def issue(j):
+            j0, j1 = widths[j]
+            buf = bufs[j]
+            if self.rank == src and buf is not b:
+                buf.copy_(b[:, j0:j1])
+            return dist.broadcast(buf, src=src, group=self.group, async_op=True), buf
+
+        # The first transfer is issued before A is packed, so packing A (no
+        # dependence on B) runs while panel 0 crosses NVLink.
+        pending = issue(0)
+        pa = K.pack_a(a_rows, self.mode)
+        for j in range(panels):
+            work, buf = pending
+            work.wait()  # the compute stream waits for panel j
+            if j + 1 < panels:
+                pending = issue(j + 1)  # panel j+1 overlaps panel j's GEMM
+            j0, j1 = widths[j]
+            packed_b = K.pack_b(buf, self.mode,
+                                out=packed_b.buf if packed_b is not None else None)
+            K.sgemm_packed(pa, packed_b, c[:, j0:j1], alpha=alpha,
+                           bias=bias[j0:j1] if bias is not None else None, relu=relu)
+        return c
 
     def gather_rows(self, c_rows: torch.Tensor, m: int) -> torch.Tensor:
         """All-gathers the row blocks into the full [m, n] C on every rank."""

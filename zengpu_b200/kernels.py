@@ -118,3 +118,69 @@ def kernel_status() -> int:
     code = C.c_uint32(0)
     check(L.load().zg_kernel_status(C.byref(code)))
     return int(code.value)
+
+
+# ---- packed operands (zg_sgemm_pack_*, zg_sgemm_packed) ----------------------------
+class Packed:
+    """An operand packed for one GEMM mode: the planes its kernel reads."""
+
+    def __init__(self, mode: int, operand: int, outer: int, k: int, buf: torch.Tensor):
+        self.mode, self.operand, self.outer, self.k, self.buf = int(mode), operand, outer, k, buf
+
+
+def pack_bytes(mode: int, operand: int, outer: int, k: int) -> int:
+    return int(L.load().zg_sgemm_pack_bytes(int(mode), operand, outer, k))
+
+
+def _pack_buffer(nbytes: int, device, out: torch.Tensor | None) -> torch.Tensor:
+    if out is not None and out.numel() >= nbytes and out.data_ptr() % 256 == 0:
+        return out
+    return torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+
+
+def _pitch(t: torch.Tensor) -> int:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError("expected a 2-D float32 CUDA tensor with unit column stride")
+    return t.stride(0)
+
+
+def pack_a(a: torch.Tensor, mode: int = GemmMode.TF32X3, out: torch.Tensor | None = None) -> Packed:
+    """Packs A [m, k] (any row pitch) for `mode`."""
+    if a.dtype != torch.float32 or not a.is_cuda:
+        raise ValueError("pack_a: float32 CUDA tensor expected")
+    m, k = a.shape
+    buf = _pack_buffer(pack_bytes(mode, 0, m, k), a.device, out)
+    check(L.load().zg_sgemm_pack_a(int(mode), m, k, a.data_ptr(), _pitch(a), buf.data_ptr(),
+                                   buf.numel(), _stream(a)))
+    return Packed(mode, 0, m, k, buf)
+
+
+def pack_b(b: torch.Tensor, mode: int = GemmMode.TF32X3, out: torch.Tensor | None = None) -> Packed:
+    """Packs B [k, n] (any row pitch) for `mode`."""
+    if b.dtype != torch.float32 or not b.is_cuda:
+        raise ValueError("pack_b: float32 CUDA tensor expected")
+    k, n = b.shape
+    buf = _pack_buffer(pack_bytes(mode, 1, n, k), b.device, out)
+    check(L.load().zg_sgemm_pack_b(int(mode), k, n, b.data_ptr(), _pitch(b), buf.data_ptr(),
+                                   buf.numel(), _stream(b)))
+    return Packed(mode, 1, n, k, buf)
+
+
+def sgemm_packed(pa: Packed, pb: Packed, c: torch.Tensor | None = None, alpha: float = 1.0,
+                 bias: torch.Tensor | None = None, relu: bool = False) -> torch.Tensor:
+    """C = epilogue(alpha * A @ B) from packed operands; `c` may be a column
+    panel view of a larger row-major matrix (row pitch = c.stride(0))."""
+    if pa.mode != pb.mode or pa.k != pb.k or pa.operand != 0 or pb.operand != 1:
+        raise ValueError("sgemm_packed: operands packed for different GEMMs")
+    m, n, k = pa.outer, pb.outer, pa.k
+    if c is None:
+        c = torch.empty((m, n), dtype=torch.float32, device=pa.buf.device)
+    if tuple(c.shape) != (m, n) or c.dtype != torch.float32:
+        raise ValueError(f"sgemm_packed: C must be float32 [{m}, {n}]")
+    if bias is not None:
+        _f32_cuda(bias)
+    check(L.load().zg_sgemm_packed(pa.mode, m, n, k, float(alpha), pa.buf.data_ptr(),
+                                   pb.buf.data_ptr(), c.data_ptr(), _pitch(c),
+                                   bias.data_ptr() if bias is not None else None,
+                                   1 if relu else 0, _stream(c)))
+    return c

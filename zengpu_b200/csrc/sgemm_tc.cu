@@ -30,6 +30,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdint>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 
@@ -123,11 +124,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
-    int m_tile, n_tile;
-    tile_coords(blockIdx.x, mt, nt, m_tile, n_tile);
-    const int m0 = m_tile * BM, n0 = n_tile * BN;
+    const int num_tiles = mt * nt;
     const int nkb = (K + BK - 1) / BK;
     const int nchunks = (nkb + Cfg::KB_PER_CHUNK - 1) / Cfg::KB_PER_CHUNK;
+    // Persistent: CTA b owns tiles b, b + gridDim.x, ... in grouped raster order.
+    auto tile_origin = [&](int t, int& m0, int& n0) {
+        int mi, ni;
+        tile_coords(t, mt, nt, mi, ni);
+        m0 = mi * BM;
+        n0 = ni * BN;
+    };
 
     auto a_plane = [&](int s, int p) { return smem + s * Cfg::STAGE_BYTES + p * Cfg::A_BYTES; };
     auto b_plane = [&](int s, int p) {
@@ -161,72 +167,85 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            int issued = 0;
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % STAGES;
-                const uint32_t ph = (kb / STAGES) & 1;
-                if (!mbar_wait_bounded(&empty[s], ph ^ 1, &g_status, kErrTcProducer)) break;
-                mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
-                const int k0 = kb * BK;
-                for (int p = 0; p < kPlanes; ++p) {
-                    tma_load_2d(a_plane(s, p), &maps.a[p], k0, m0, &full[s]);
-                    tma_load_2d(b_plane(s, p), &maps.b[p], k0, n0, &full[s]);
+            int it = 0;  // k-blocks issued by this CTA over all its tiles
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                int m0, n0;
+                tile_origin(t, m0, n0);
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    if (!mbar_wait_bounded(&empty[s], ph ^ 1, &g_status, kErrTcProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+                    const int k0 = kb * BK;
+                    for (int p = 0; p < kPlanes; ++p) {
+                        tma_load_2d(a_plane(s, p), &maps.a[p], k0, m0, &full[s]);
+                        tma_load_2d(b_plane(s, p), &maps.b[p], k0, n0, &full[s]);
+                    }
                 }
-                issued = kb + 1;
             }
             // Make sure no copy is still landing in shared memory at exit.
-            const int first = issued > STAGES ? issued - STAGES : 0;
-            for (int kb = first; kb < issued; ++kb)
-                mbar_wait_bounded(&full[kb % STAGES], (kb / STAGES) & 1, &g_status, kErrTcDrain);
+            const int first = it > STAGES ? it - STAGES : 0;
+            for (int i = first; i < it; ++i)
+                mbar_wait_bounded(&full[i % STAGES], (i / STAGES) & 1, &g_status, kErrTcDrain);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             bool ok = true;
-            for (int j = 0; j < nchunks && ok; ++j) {
-                const int buf = j & 1;
-                const uint32_t d_tmem = tmem_base + buf * BN;
-                if (j >= 2 && !mbar_wait_bounded(&acc_empty[buf], ((j >> 1) - 1) & 1, &g_status,
-                                                 kErrTcMma)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const int kb0 = j * Cfg::KB_PER_CHUNK;
-                const int kb1 = min(nkb, kb0 + Cfg::KB_PER_CHUNK);
-                for (int kb = kb0; kb < kb1; ++kb) {
-                    const int s = kb % STAGES;
-                    const uint32_t ph = (kb / STAGES) & 1;
-                    if (!mbar_wait_bounded(&full[s], ph, &g_status, kErrTcMma)) {
+            int it = 0;  // k-blocks consumed
+            int cj = 0;  // accumulation chunks issued (alternating TMEM buffers)
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                for (int j = 0; j < nchunks && ok; ++j, ++cj) {
+                    const int buf = cj & 1;
+                    const uint32_t d_tmem = tmem_base + buf * BN;
+                    if (cj >= 2 && !mbar_wait_bounded(&acc_empty[buf], ((cj >> 1) - 1) & 1,
+                                                      &g_status, kErrTcMma)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(a_plane(s, 0));
-                    const uint32_t b0 = smem_u32(b_plane(s, 0));
-#pragma unroll
-                    for (int kk = 0; kk < BK / 8; ++kk) {
-                        // Advance 8 f32 (32 bytes) inside the swizzled K row.
-                        const uint64_t ahi = umma_desc(a0 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
-                        const uint64_t bhi = umma_desc(b0 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
-                        const uint32_t acc0 = (kb != kb0 || kk != 0) ? 1u : 0u;
-                        if (kPlanes == 2) {
-                            const uint32_t a1 = smem_u32(a_plane(s, 1));
-                            const uint32_t b1 = smem_u32(b_plane(s, 1));
-                            const uint64_t alo =
-                                umma_desc(a1 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
-                            const uint64_t blo =
-                                umma_desc(b1 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
-                            mma_tf32_ss(d_tmem, alo, bhi, kIdesc, acc0);
-                            mma_tf32_ss(d_tmem, ahi, blo, kIdesc, 1u);
-                            mma_tf32_ss(d_tmem, ahi, bhi, kIdesc, 1u);
-                        } else {
-                            mma_tf32_ss(d_tmem, ahi, bhi, kIdesc, acc0);
+                    const int kb0 = j * Cfg::KB_PER_CHUNK;
+                    const int kb1 = min(nkb, kb0 + Cfg::KB_PER_CHUNK);
+                    for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                        const int s = it % STAGES;
+                        const uint32_t ph = (it / STAGES) & 1;
+                        if (!mbar_wait_bounded(&full[s], ph, &g_status, kErrTcMma)) {
+                            ok = false;
+                            break;
                         }
+                        tc_fence_after();
+                        const uint32_t a0 = smem_u32(a_plane(s, 0));
+                        const uint32_t b0 = smem_u32(b_plane(s, 0));
+#pragma unroll
+                        for (int kk = 0; kk < BK / 8; ++kk) {
+                            // Advance 8 f32 (32 bytes) inside the swizzled K row.
+                            const uint64_t ahi =
+                                umma_desc(a0 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
+                            const uint64_t bhi =
+                                umma_desc(b0 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
+                            const uint32_t acc0 = (kb != kb0 || kk != 0) ? 1u : 0u;
+                            if (kPlanes == 2) {
+                                const uint32_t a1 = smem_u32(a_plane(s, 1));
+                                const uint32_t b1 = smem_u32(b_plane(s, 1));
+                                const uint64_t alo =
+                                    umma_desc(a1 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
+                                const uint64_t blo =
+                                    umma_desc(b1 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
+                                mma_tf32_ss(d_tmem, alo, bhi, kIdesc, acc0);
+                                mma_tf32_ss(d_tmem, ahi, blo, kIdesc, 1u);
+                                mma_tf32_ss(d_tmem, ahi, bhi, kIdesc, 1u);
+                            } else {
+                                mma_tf32_ss(d_tmem, ahi, bhi, kIdesc, acc0);
+                            }
+                        }
+                        mma_commit(&empty[s]);  // stage s free once these MMAs finish
                     }
-                    mma_commit(&empty[s]);  // stage s free once these MMAs finish
+                    if (ok) mma_commit(&acc_full[buf]);  // chunk complete in buffer buf
                 }
-                if (ok) mma_commit(&acc_full[buf]);  // chunk j complete in buffer buf
             }
             if (!ok) {
                 mma_commit(drain);
@@ -235,54 +254,60 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else {
         // ---------------- epilogue (warps 2..9) ----------------
-        const int q = warp & 3;                 // TMEM lane quarter this warp may access
-        const int half = (warp - 2) >> 2;        // 128-column half of the tile
-        const int row = m0 + q * 32 + lane;
+        const int q = warp & 3;             // TMEM lane quarter this warp may access
+        const int half = (warp - 2) >> 2;   // 128-column half of the tile
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + half * 128;
-        float acc[128];
-#pragma unroll
-        for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
         bool ok = true;
-        for (int j = 0; j < nchunks; ++j) {
-            const int buf = j & 1;
-            if (!mbar_wait_bounded(&acc_full[buf], (j >> 1) & 1, &g_status, kErrTcEpilogue)) {
-                ok = false;
-                break;
+        int cj = 0;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+            int m0, n0;
+            tile_origin(t, m0, n0);
+            const int row = m0 + q * 32 + lane;
+            float acc[128];
+#pragma unroll
+            for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+            for (int j = 0; j < nchunks; ++j, ++cj) {
+                const int buf = cj & 1;
+                if (!mbar_wait_bounded(&acc_full[buf], (cj >> 1) & 1, &g_status,
+                                       kErrTcEpilogue)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(lane_base + buf * BN + cc * 32, r);
+#pragma unroll
+                    for (int u = 0; u < 32; ++u) acc[cc * 32 + u] += __uint_as_float(r[u]);
+                }
+                tc_fence_before();
+                mbar_arrive(&acc_empty[buf]);
             }
-            tc_fence_after();
+            if (ok && row < M) {
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(lane_base + buf * BN + cc * 32, r);
+                for (int cc = 0; cc < 4; ++cc) {
+                    const int col0 = n0 + half * 128 + cc * 32;
+                    if (col0 < N) {
+                        float v[32];
 #pragma unroll
-                for (int t = 0; t < 32; ++t) acc[cc * 32 + t] += __uint_as_float(r[t]);
-            }
-            tc_fence_before();
-            mbar_arrive(&acc_empty[buf]);
-        }
-        if (ok && row < M) {
+                        for (int u = 0; u < 32; ++u) {
+                            float x = __fmul_rn(alpha, acc[cc * 32 + u]);
+                            if (bias) x = __fadd_rn(x, col0 + u < N ? __ldg(bias + col0 + u) : 0.0f);
+                            if (relu) x = relu1(x);
+                            v[u] = x;
+                        }
+                        float* dst = C + static_cast<int64_t>(row) * ldc + col0;
+                        if (vec_c && col0 + 32 <= N) {
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                const int col0 = n0 + half * 128 + cc * 32;
-                if (col0 < N) {
-                    float v[32];
+                            for (int u = 0; u < 32; u += 4)
+                                *reinterpret_cast<float4*>(dst + u) =
+                                    make_float4(v[u], v[u + 1], v[u + 2], v[u + 3]);
+                        } else {
 #pragma unroll
-                    for (int t = 0; t < 32; ++t) {
-                        float x = __fmul_rn(alpha, acc[cc * 32 + t]);
-                        if (bias) x = __fadd_rn(x, col0 + t < N ? __ldg(bias + col0 + t) : 0.0f);
-                        if (relu) x = relu1(x);
-                        v[t] = x;
-                    }
-                    float* dst = C + static_cast<int64_t>(row) * ldc + col0;
-                    if (vec_c && col0 + 32 <= N) {
-#pragma unroll
-                        for (int t = 0; t < 32; t += 4)
-                            *reinterpret_cast<float4*>(dst + t) =
-                                make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
-                    } else {
-#pragma unroll
-                        for (int t = 0; t < 32; ++t)
-                            if (col0 + t < N) dst[t] = v[t];
+                            for (int u = 0; u < 32; ++u)
+                                if (col0 + u < N) dst[u] = v[u];
+                        }
                     }
                 }
             }
@@ -489,8 +514,13 @@ int launch_tc(const TcMaps& maps, int M, int N, int K, float alpha, float* C, in
     if (attr_err != cudaSuccess) return cuda_status(attr_err, "sgemm_tc smem attribute");
     const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
     const int vec_c = (ldc % 4 == 0) && aligned16(C);
-    sgemm_tc_kernel<kPlanes><<<mt * nt, kTcThreads, Cfg::SMEM_BYTES, s>>>(maps, M, N, K, alpha, C,
-                                                                         ldc, bias, relu, vec_c);
+    // Persistent grid: one CTA per SM (the smem footprint allows no more).
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = std::min(mt * nt, std::max(sms, 1));
+    sgemm_tc_kernel<kPlanes><<<grid, kTcThreads, Cfg::SMEM_BYTES, s>>>(maps, M, N, K, alpha, C,
+                                                                      ldc, bias, relu, vec_c);
     return cuda_status(cudaGetLastError(), "sgemm_tc");
 }
 

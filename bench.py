@@ -48,7 +48,8 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 #   --set full -k regex:sgemm_tc_kernel on `bench.py --steps 1 --warmup 3 --no-extras`
 #   --section MemoryWorkloadAnalysis -k regex:stream_vec_kernel on the elementwise workload
 NCU_TRAFFIC = {
-    ("gemm", "tf32x3", 8192): 5.841e9,
+    ("gemm", "tf32bf16", 8192): 4.841e9,
+    ("gemm", "tf32x3", 8192): 4.869e9,
     ("elementwise", "add", 1 << 28): 3.188e9,
 }
 
@@ -204,7 +205,9 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["gemm", "mlp", "sharded", "elementwise"],
                     default="gemm")
-    ap.add_argument("--mode", choices=["tf32x3", "tf32", "simt"], default="tf32x3")
+    ap.add_argument("--mode", choices=["tf32x3", "tf32", "simt", "tf32bf16"], default="tf32bf16",
+                    help="GEMM arithmetic; tf32bf16 and tf32x3 are the fp32-accurate "
+                         "(rel-Frobenius <= 1e-5) tensor-core modes")
     ap.add_argument("--size", type=int, default=8192)
     ap.add_argument("--panels", type=int, default=1,
                     help="N > 1: column panels of the B broadcast (1 = whole B, overlapped "
@@ -264,7 +267,7 @@ def ours(args, rank: int, local_rank: int, world: int) -> int:
                                 device_id=dev)
     peaks, peak_src = load_peaks()
     mode = {"tf32x3": zg.GemmMode.TF32X3, "tf32": zg.GemmMode.TF32,
-            "simt": zg.GemmMode.SIMT_FP32}[args.mode]
+            "simt": zg.GemmMode.SIMT_FP32, "tf32bf16": zg.GemmMode.TF32_BF16X2}[args.mode]
     try:
         if args.workload == "mlp":
             line = mlp_workload(args, torch, zg, K, mode, peaks, peak_src, world)
@@ -381,14 +384,21 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
     if K.kernel_status() != 0:
         raise RuntimeError("bounded on-device wait expired during timing")
 
+    accuracy = sampled_accuracy(torch, a, b, c, mode, rank, world)
+    other = {}
+    if not args.no_extras and args.workload == "gemm" and mode == zg.GemmMode.TF32_BF16X2:
+        other["tf32x3"] = kernel_only(torch, lib, zg.GemmMode.TF32X3, a, b, c, m_local, n, k, sp,
+                                      stream, dist, world)
     total_flops = 2.0 * m_total * n * k
     value = total_flops / (ms * 1e-3) / 1e12
     rank_flops = 2.0 * m_local * n * k
     achieved = rank_flops / (kern_ms * 1e-3) / 1e12
     tf32_peak = peaks["bf16_tflops"] / 2.0
     fp32_simt_peak = 148 * 128 * 2 * 1.965e9 / 1e12  # SMs x FP32 lanes x FMA x max clock
+    # TF32_BF16X2: one tf32 product + two bf16 products at twice the tf32 rate
     peak = {zg.GemmMode.TF32X3: tf32_peak / 3.0, zg.GemmMode.TF32: tf32_peak,
-            zg.GemmMode.SIMT_FP32: fp32_simt_peak}[mode]
+            zg.GemmMode.SIMT_FP32: fp32_simt_peak,
+            zg.GemmMode.TF32_BF16X2: tf32_peak / 2.0}[mode]
     # N = 1: TF32X3 split(A) + transpose-split(B) + tcgen05 kernel; TF32:
     # transpose(B) (+ a pitched copy of A when k % 4 != 0) + kernel; SIMT: one.
     # N > 1: pack(A) + per column panel pack(B panel) + kernel.
@@ -396,7 +406,7 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
         launches_per_step = 1 + 2 * panels
     else:
         launches_per_step = {zg.GemmMode.TF32X3: 3, zg.GemmMode.TF32: 2 + (k % 4 != 0),
-                             zg.GemmMode.SIMT_FP32: 1}[mode]
+                             zg.GemmMode.SIMT_FP32: 1, zg.GemmMode.TF32_BF16X2: 3}[mode]
 
     extras = {}
     e2e = None
@@ -419,7 +429,7 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
                                      if world > 1 else ")"),
                    "l2": "inputs larger than L2: A, B 256 MiB each, plus 1 GiB of hi/lo planes"},
         "roofline": {"bound": "tensor" if mode != zg.GemmMode.SIMT_FP32 else "fp32",
-                     "kernel": f"sgemm_tc_kernel<{2 if mode == 1 else 1}>"
+                     "kernel": f"sgemm_tc_kernel<{ {1: 2, 2: 1, 3: 3}.get(int(mode), 0)}>"
                      if mode != zg.GemmMode.SIMT_FP32 else "sgemm_simt_kernel",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak,
@@ -428,13 +438,19 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
                      "algorithmic_bytes": algorithmic_bytes(mode, m_local, n, k),
                      "kernel_ms": kern_ms,
                      "peak_basis": (f"{peak_src} bf16 {peaks['bf16_tflops']} TFLOP/s / 2 (tf32 "
-                                    "rate)" + (" / 3 (MMAs per useful product)"
-                                               if mode == zg.GemmMode.TF32X3 else ""))
+                                    "rate)" + {zg.GemmMode.TF32X3: " / 3 (tf32 MMAs per useful "
+                                               "product)",
+                                               zg.GemmMode.TF32_BF16X2: " / 2 (one tf32 + two "
+                                               "half-cost bf16 MMAs per useful product)"}
+                                    .get(mode, ""))
                      if mode != zg.GemmMode.SIMT_FP32 else
                      "nominal FP32 SIMT: 148 SMs x 128 lanes x 2 flop x 1965 MHz"},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
     }
+    line["accuracy"] = accuracy
+    if other:
+        line["other_modes"] = other
     if e2e is not None:
         line["e2e"] = e2e
     if cpu is not None:
@@ -444,12 +460,55 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
     return line
 
 
+def sampled_accuracy(torch, a, b, c, mode, rank, world) -> dict:
+    """Relative Frobenius error of a 256 x 256 block of this rank's C against a
+    float64 product of the same operands (numpy on the host)."""
+    import numpy as np
+    import zengpu_b200 as zg
+    r0 = min(1000, max(a.shape[0] - 256, 0))
+    c0 = min(3000, max(b.shape[1] - 256, 0))
+    rows = a[r0:r0 + 256].double().cpu().numpy()
+    cols = b[:, c0:c0 + 256].double().cpu().numpy()
+    if world > 1 and rank != 0:
+        return {"skipped": "B on this rank is not the broadcast value after timing"}
+    ref = rows @ cols
+    got = c[r0:r0 + 256, c0:c0 + 256].double().cpu().numpy()
+    err = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
+    bar = 5e-3 if mode == zg.GemmMode.TF32 else 1e-5
+    return {"rel_fro_vs_fp64": err, "bar": bar, "block": [r0, c0, 256, 256],
+            "within_bar": err <= bar}
+
+
+def kernel_only(torch, lib, mode, a, b, c, m, n, k, sp, stream, dist, world, reps: int = 5):
+    """Device time of one more mode's tensor-core kernel on the same operands."""
+    import zengpu_b200 as zg
+    from zengpu_b200 import kernels as K
+    ws = torch.empty(max(K.workspace_bytes(mode, m, n, k), 256), dtype=torch.uint8,
+                     device="cuda")
+    zg.api.check(lib.zg_sgemm_prepare(int(mode), m, n, k, a.data_ptr(), b.data_ptr(),
+                                      ws.data_ptr(), ws.numel(), sp))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(reps + 2)]
+    for e0, e1 in evs:
+        e0.record(stream)
+        zg.api.check(lib.zg_sgemm_compute(int(mode), m, n, k, 1.0, a.data_ptr(), b.data_ptr(),
+                                          c.data_ptr(), None, 0, ws.data_ptr(), ws.numel(), sp))
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs[2:])
+    acc = sampled_accuracy(torch, a, b, c, mode, 0, 1)
+    del ws
+    torch.cuda.empty_cache()
+    return {"kernel_ms": ms, "kernel_tflops": 2.0 * m * n * k / (ms * 1e-3) / 1e12,
+            "accuracy": acc}
+
+
 def algorithmic_bytes(mode: int, m: int, n: int, k: int) -> int:
     """Bytes the GEMM kernel must move once: its operand planes in, C out."""
-    planes = 2 if mode == 1 else 1
     if mode == 0:  # SIMT reads A and B directly
         return 4 * (m * k + k * n + m * n)
-    return 4 * planes * (m * k + n * k) + 4 * m * n
+    per_elem = {1: 8, 2: 4, 3: 8}[int(mode)]  # tf32 hi+lo / f32 / tf32 + 2 bf16
+    return per_elem * (m * k + n * k) + 4 * m * n
 
 
 def gemm_e2e(args, torch, dist, zg, K, mode, m_local, n, k, m_total, world, local_rank):

@@ -94,10 +94,14 @@ typedef struct zg_handle {
 
 /* GEMM arithmetic.  SIMT_FP32: exact-fp32 CUDA-core SGEMM (FMA, rel-Frobenius
  * <= 1e-5).  TF32X3: tcgen05 tensor cores, split-precision hi*hi + hi*lo +
- * lo*hi (rel-Frobenius <= 1e-5).  TF32: one tcgen05 TF32 pass (<= 5e-3). */
+ * lo*hi, three TF32 products (rel-Frobenius <= 1e-5).  TF32: one tcgen05 TF32
+ * pass (<= 5e-3).  TF32_BF16X2: the same split with the two small correction
+ * products in bf16 (twice the TF32 rate), 2/3 of TF32X3's tensor time
+ * (rel-Frobenius <= 1e-5). */
 #define ZG_GEMM_SIMT_FP32 0
 #define ZG_GEMM_TF32X3 1
 #define ZG_GEMM_TF32 2
+#define ZG_GEMM_TF32_BF16X2 3
 
 /* ======================================================================
  * 1. Device runtime
@@ -303,9 +307,10 @@ int zg_saxpy_f32(float alpha, const float *x, float *y, uint64_t n, void *stream
 /* x *= alpha  (SCAL_ZSL, zengpu-blas/src/level1.rs:23-32) */
 int zg_sscal_f32(float alpha, float *x, uint64_t n, void *stream);
 
-/* Scratch bytes zg_sgemm_f32 needs for (mode, m, n, k): the TF32X3 mode
- * stores tf32 hi/lo planes of A and B; the TF32 mode stores pitch-padded
- * copies when k or n is not a multiple of 4; SIMT needs none. */
+/* Scratch bytes zg_sgemm_f32 needs for (mode, m, n, k): the operand planes
+ * the tensor-core kernel reads (tf32 / bf16 planes of A, and of B transposed
+ * to K-major; TF32 reads A directly when k is a multiple of 4); SIMT needs
+ * none. */
 uint64_t zg_sgemm_workspace_bytes(int mode, int m, int n, int k);
 /* C[m,n] = epilogue(alpha * A[m,k] @ B[k,n]), all row-major f32.
  * epilogue: identity, or relu(x + bias[col]) when `bias` is non-NULL and

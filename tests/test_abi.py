@@ -52,10 +52,12 @@ def test_no_device_is_reported_not_crashed():
 def test_workspace_bytes():
     lib = zg.load_library()
     assert lib.zg_sgemm_workspace_bytes(0, 1024, 1024, 1024) == 0
-    # TF32X3: hi/lo planes of A (m x k) and of B transposed (n x k), k pitch rounded to 4
+    # TF32X3 / TF32_BF16X2: A (m rows) and B transposed (n rows), each 16-k block
+    # one 128-byte row of interleaved terms (k padded to 16), 256-byte aligned
     assert lib.zg_sgemm_workspace_bytes(1, 8192, 8192, 8192) == 4 * 8192 * 8192 * 4
-    assert lib.zg_sgemm_workspace_bytes(1, 17, 9, 33) == 2 * 256 * ((17 * 36 * 4 + 255) // 256) + \
-        2 * 256 * ((9 * 36 * 4 + 255) // 256)
+    assert lib.zg_sgemm_workspace_bytes(3, 8192, 8192, 8192) == 4 * 8192 * 8192 * 4
+    assert lib.zg_sgemm_workspace_bytes(1, 17, 9, 33) == 256 * ((17 * 96 * 4 + 255) // 256) + \
+        256 * ((9 * 96 * 4 + 255) // 256)
     # TF32: the K-major copy of B, plus a pitched copy of A when k % 4 != 0
     assert lib.zg_sgemm_workspace_bytes(2, 64, 64, 64) == 64 * 64 * 4
     assert lib.zg_sgemm_workspace_bytes(2, 17, 9, 33) == 256 * ((17 * 36 * 4 + 255) // 256) + \

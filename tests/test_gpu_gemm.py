@@ -13,8 +13,9 @@ from zengpu_b200 import kernels as K
 
 pytestmark = pytest.mark.gpu
 
-MODES = [zg.GemmMode.SIMT_FP32, zg.GemmMode.TF32X3, zg.GemmMode.TF32]
-TOL = {zg.GemmMode.SIMT_FP32: 1e-5, zg.GemmMode.TF32X3: 1e-5, zg.GemmMode.TF32: 5e-3}
+MODES = [zg.GemmMode.SIMT_FP32, zg.GemmMode.TF32X3, zg.GemmMode.TF32, zg.GemmMode.TF32_BF16X2]
+TOL = {zg.GemmMode.SIMT_FP32: 1e-5, zg.GemmMode.TF32X3: 1e-5, zg.GemmMode.TF32: 5e-3,
+       zg.GemmMode.TF32_BF16X2: 1e-5}
 
 
 def bits(x) -> np.ndarray:

@@ -102,6 +102,7 @@ class GemmMode(enum.IntEnum):
     SIMT_FP32 = 0
     TF32X3 = 1
     TF32 = 2
+    TF32_BF16X2 = 3
 
 
 class ShaderKind(enum.IntEnum):

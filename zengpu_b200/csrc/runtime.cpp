@@ -247,6 +247,7 @@ int default_gemm_mode() {
     std::string s(e);
     if (s == "simt" || s == "simt_fp32" || s == "fp32") return ZG_GEMM_SIMT_FP32;
     if (s == "tf32") return ZG_GEMM_TF32;
+    if (s == "tf32bf16" || s == "tf32_bf16x2") return ZG_GEMM_TF32_BF16X2;
     return ZG_GEMM_TF32X3;
 }
 
@@ -810,6 +811,7 @@ extern "C" int zg_pipeline_create(zg_device* dev, zg_handle shader, const char* 
             {"sgemm_f32.simt", kSgemmF32, ZG_GEMM_SIMT_FP32},
             {"sgemm_f32.tf32x3", kSgemmF32, ZG_GEMM_TF32X3},
             {"sgemm_f32.tf32", kSgemmF32, ZG_GEMM_TF32},
+            {"sgemm_f32.tf32bf16", kSgemmF32, ZG_GEMM_TF32_BF16X2},
             {"sgemm_bias_relu_f32", kSgemmBiasReluF32, -1},
         };
         for (auto& t : table)
@@ -1367,7 +1369,8 @@ extern "C" int zg_gemm_sgemm_host(const zg_gemm_kernel* kern, zg_device* dev, fl
     if (m == 0 || n == 0) return ZG_OK;
     if (!c || (k > 0 && (!a || !b))) return set_error(ZG_ERR_DISPATCH, "sgemm_host: null host pointer");
     const int mode = kern->mode;
-    if (mode != ZG_GEMM_SIMT_FP32 && mode != ZG_GEMM_TF32X3 && mode != ZG_GEMM_TF32)
+    if (mode != ZG_GEMM_SIMT_FP32 && mode != ZG_GEMM_TF32X3 && mode != ZG_GEMM_TF32 &&
+        mode != ZG_GEMM_TF32_BF16X2)
         return set_error(ZG_ERR_DISPATCH, "sgemm: unknown mode %d", mode);
     std::lock_guard<std::recursive_mutex> lk(dev->mu);
     int rc = set_device(dev);
@@ -1377,30 +1380,25 @@ extern "C" int zg_gemm_sgemm_host(const zg_gemm_kernel* kern, zg_device* dev, fl
                          "sgemm_host cannot run while an asynchronous submission is pending");
     if ((rc = ensure_copy_streams(dev))) return rc;
     const int M = static_cast<int>(m), N = static_cast<int>(n), K = static_cast<int>(k);
-    const int64_t kp = gemm_plane_pitch(K);
     const bool a_planes = K > 0 && gemm_a_needs_planes(mode, K);
     const bool b_planes = K > 0 && gemm_b_needs_planes(mode);
-    const bool lo = mode == ZG_GEMM_TF32X3;
-    // Staging layout: A, B, C, bias, A planes (hi, lo), B^T planes (hi, lo).
+    // Staging layout: A, B, C, bias, A planes, B^T planes.
     uint64_t off = 0;
     const uint64_t o_a = off; off += align256(uint64_t(M) * K * 4);
     const uint64_t o_b = off; off += align256(uint64_t(K) * N * 4);
     const uint64_t o_c = off; off += align256(uint64_t(M) * N * 4);
     const uint64_t o_bias = off; off += align256(uint64_t(N) * 4);
-    const uint64_t o_ah = off; off += a_planes ? align256(uint64_t(M) * kp * 4) : 0;
-    const uint64_t o_al = off; off += a_planes && lo ? align256(uint64_t(M) * kp * 4) : 0;
-    const uint64_t o_bh = off; off += b_planes ? align256(uint64_t(N) * kp * 4) : 0;
-    const uint64_t o_bl = off; off += b_planes && lo ? align256(uint64_t(N) * kp * 4) : 0;
+    const uint64_t o_ap = off; off += a_planes ? gemm_planes_bytes(mode, M, K) : 0;
+    const uint64_t o_bp = off; off += b_planes ? gemm_planes_bytes(mode, N, K) : 0;
     if ((rc = ensure_staging(dev, off))) return rc;
     uint8_t* base = static_cast<uint8_t*>(dev->staging);
     float* dA = reinterpret_cast<float*>(base + o_a);
     float* dB = reinterpret_cast<float*>(base + o_b);
     float* dC = reinterpret_cast<float*>(base + o_c);
     float* dBias = reinterpret_cast<float*>(base + o_bias);
-    float* ah = reinterpret_cast<float*>(base + o_ah);
-    float* al = lo ? reinterpret_cast<float*>(base + o_al) : nullptr;
-    float* bh = reinterpret_cast<float*>(base + o_bh);
-    float* bl = lo ? reinterpret_cast<float*>(base + o_bl) : nullptr;
+    const OperandView a_ps = a_planes ? gemm_carve_planes(base + o_ap, mode, M, K) : OperandView{};
+    const OperandView b_ps = b_planes ? gemm_carve_planes(base + o_bp, mode, N, K)
+                                      : gemm_raw_operand(dB, N);
 
     // Row panels of A / C: large enough to keep the GEMM efficient, small
     // enough that uploading A, computing and downloading C overlap.
@@ -1426,7 +1424,7 @@ extern "C" int zg_gemm_sgemm_host(const zg_gemm_kernel* kern, zg_device* dev, fl
         if (!rc) rc = cuda_status(cudaEventRecord(ev[1 + p], dev->h2d), "event");
     }
     if (!rc) rc = cuda_status(cudaStreamWaitEvent(comp, ev[0], 0), "wait B");
-    if (!rc && b_planes) rc = gemm_prep_b(mode, K, N, dB, N, bh, bl, kp, comp);
+    if (!rc && b_planes) rc = gemm_prep_b(mode, K, N, dB, N, b_ps, comp);
     for (int p = 0; p < panels && !rc; ++p) {
         const int r0 = p * rows, nr = std::min(rows, M - r0);
         if ((rc = cuda_status(cudaStreamWaitEvent(comp, ev[1 + p], 0), "wait A panel"))) break;
@@ -1436,21 +1434,9 @@ extern "C" int zg_gemm_sgemm_host(const zg_gemm_kernel* kern, zg_device* dev, fl
                               relu, nullptr, 0, comp);
         } else {
             const float* ap = dA + int64_t(r0) * K;
-            if (a_planes &&
-                (rc = gemm_prep_a(mode, nr, K, ap, K, ah + int64_t(r0) * kp,
-                                  lo ? al + int64_t(r0) * kp : nullptr, kp, comp)))
-                break;
-            GemmOperands op{mode, ap, nullptr, K, dB, nullptr, N};
-            if (a_planes) {
-                op.a_hi = ah + int64_t(r0) * kp;
-                op.a_lo = lo ? al + int64_t(r0) * kp : nullptr;
-                op.lda = kp;
-            }
-            if (b_planes) {
-                op.b_hi = bh;
-                op.b_lo = bl;
-                op.ldb = kp;
-            }
+            const OperandView panel_ps = a_planes ? gemm_offset_rows(a_ps, r0) : OperandView{};
+            if (a_planes && (rc = gemm_prep_a(mode, nr, K, ap, K, panel_ps, comp))) break;
+            GemmOperands op{mode, a_planes ? panel_ps : gemm_raw_operand(ap, K), b_ps};
             rc = gemm_run(op, nr, N, K, alpha, cp, N, bias ? dBias : nullptr, relu, comp);
         }
         if (!rc) rc = cuda_status(cudaEventRecord(ev[1 + panels + p], comp), "event");

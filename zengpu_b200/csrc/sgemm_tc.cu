@@ -2,35 +2,51 @@
 // dispatcher behind zg_sgemm_f32 (the kernel contract of GEMM_PTX's entry
 // `main(a, b, c, m, n, k, alpha)`, zengpu-blas/src/level3.rs:35-90).
 //
-// Two tensor-core modes share one kernel template:
-//   TF32    one kind::tf32 MMA per k-step on the raw f32 operands;
-//   TF32X3  split precision: x = hi + lo with hi = tf32(x), lo = tf32(x - hi)
-//           (round-to-nearest both), D += A_lo*B_hi + A_hi*B_lo + A_hi*B_hi;
-//           the dropped lo*lo term is ~2^-22 relative, so the result keeps
-//           fp32-class accuracy.  A pre-pass writes the hi/lo planes.
+// Three tensor-core modes share one kernel template (S = planes per operand):
+//   TF32 (S=1)         one kind::tf32 MMA per k-step on f32 operands;
+//   TF32X3 (S=2)       split precision: x = hi + lo, hi = tf32(x),
+//                      lo = tf32(x - hi) (round to nearest both);
+//                      D += A_lo*B_hi + A_hi*B_lo + A_hi*B_hi, three
+//                      kind::tf32 MMAs; the dropped lo*lo term is ~2^-22;
+//   TF32_BF16X2 (S=3)  the same split, but the two correction products, which
+//                      only need ~2^-19 relative precision, run as one
+//                      kind::f16 bf16 MMA each (twice the tf32 rate):
+//                      D += bf16(A_lo)*bf16(B_hi) + bf16(A_hi)*bf16(B_lo)
+//                         + A_hi*B_hi (tf32): 2/3 of TF32X3's MMA time.
+// A pre-pass writes the operands in the layout the kernel reads: A with k
+// innermost, B transposed to K-major, and for the split modes every 16-k block
+// of a row packed into one 128-byte row holding all of that block's terms
+// (TF32X3: 16 tf32 hi | 16 tf32 lo; TF32_BF16X2: 16 tf32 hi | 16 bf16 hi |
+// 16 bf16 lo).  Full 128-byte rows keep the TMA engine at full rate: one box
+// per operand per stage, one 128-byte swizzle for every term, and each MMA
+// descriptor is an offset into the same swizzled rows.
 //
-// Kernel layout (one 128 x 256 output tile per CTA, 320 threads):
-//   warp 0      TMA producer: A tile [128 x BK] and B^T tile [256 x BK], both
-//               K-major and swizzled (B is transposed to K-major planes by the
-//               pre-pass), into a STAGES-deep mbarrier ring;
+// Kernel layout (persistent, one CTA per SM, 128 x 256 output tiles, 320
+// threads):
+//   warp 0      TMA producer: per stage one 2-D load of A [128 rows x 128 B]
+//               and one of B^T [256 rows x 128 B], 128-byte swizzled, into a
+//               4-stage mbarrier ring (48 KB per stage);
 //   warp 1      allocates 512 TMEM columns (two 128 x 256 f32 accumulators,
-//               lane = row) and one thread issues tcgen05.mma, committing each
+//               lane = row) and one thread issues the MMAs, committing each
 //               stage back to the producer and each finished k-chunk to the
 //               epilogue;
-//   warps 2-9   epilogue: two warps per TMEM lane quarter, one per 128-column
-//               half.  The tensor core's f32 accumulation truncates, so its
-//               error grows with k; the epilogue therefore drains the TMEM
-//               accumulator every kChunkK of k into f32 registers (round to
-//               nearest) while the MMA fills the other accumulator, then
+//   warps 2-9   epilogue, two warps per TMEM lane quarter (one per 128-column
+//               half).  The tensor core's f32 accumulation truncates, so its
+//               error grows with k; for the split modes the epilogue drains
+//               the TMEM accumulator every 512 of k into f32 registers (round
+//               to nearest) while the MMA fills the other accumulator, then
 //               applies alpha / bias / ReLU and stores with 128-bit writes.
+//               The chunk pipeline runs on across tiles, so a tile's final
+//               drain and store overlap the next tile's MMAs.
 // Every mbarrier wait is bounded (zg_common.cuh); an expiry sets a bit in the
 // device status word, the kernel drains its in-flight copies and MMAs, frees
 // TMEM and returns.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
-#include <cstdint>
 #include <algorithm>
+#include <cstdint>
 #include <cstring>
 #include <mutex>
 
@@ -53,26 +69,26 @@ constexpr int kEpiWarps = 8;
 constexpr int kTcThreads = 64 + 32 * kEpiWarps;  // producer, MMA, 8 epilogue warps
 constexpr uint32_t kTmemCols = 512;              // two BN-column accumulators
 
-template <int kPlanes>
+// Per-scheme stage geometry: every operand row of a stage is 128 bytes (BK
+// values of k: 32 f32 for TF32, 16 interleaved split values otherwise).
+template <int S>
 struct TcCfg {
-    static constexpr int BK = kPlanes == 1 ? 32 : 16;  // k per stage
-    static constexpr int STAGES = 4;                   // 48 KB per stage
-    static constexpr int A_BYTES = BM * BK * 4;        // one plane
-    static constexpr int B_BYTES = BN * BK * 4;        // one plane
-    static constexpr int STAGE_BYTES = kPlanes * (A_BYTES + B_BYTES);
+    static constexpr int BK = S == 1 ? 32 : 16;  // k per stage
+    static constexpr int STAGES = 4;
+    static constexpr int ROW = 128;              // bytes per operand row per stage
+    static constexpr int A_BYTES = BM * ROW;
+    static constexpr int B_BYTES = BN * ROW;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*bars*/;
-    // Both operands K-major, rows of BK*4 bytes, swizzled at that width.
-    static constexpr uint32_t LAYOUT = BK == 32 ? 2u : 4u;  // SWIZZLE_128B : SWIZZLE_64B
-    static constexpr uint32_t SBO = 8 * BK * 4;             // 8-row core-matrix group
-    // k-blocks per TMEM accumulation chunk: 512 of k for TF32X3 (keeps the
-    // truncation error of the tensor-core accumulator near 3e-6 relative);
-    // TF32 (tolerance 5e-3) accumulates the whole k range in TMEM.
-    static constexpr int KB_PER_CHUNK = kPlanes == 2 ? 512 / BK : (1 << 30);
+    // k-blocks per TMEM accumulation chunk: 512 of k for the split modes
+    // (keeps the accumulator's truncation error near 3e-6 relative); TF32
+    // (tolerance 5e-3) accumulates the whole k range in TMEM.
+    static constexpr int KB_PER_CHUNK = S >= 2 ? 512 / BK : (1 << 30);
 };
 
 struct TcMaps {
-    CUtensorMap a[2];  // hi, lo (TF32 uses a[0] only)
-    CUtensorMap b[2];
+    CUtensorMap a;
+    CUtensorMap b;
 };
 
 // UMMA shared-memory descriptor (sm100): start, leading / stride byte
@@ -85,14 +101,15 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
            (static_cast<uint64_t>(layout) << 61);
 }
 
-// Instruction descriptor, kind::tf32: D f32, A/B tf32, both K-major,
-// M = 128, N = 256.
-constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (0u << 15) | (0u << 16) |
-                            (static_cast<uint32_t>(BN >> 3) << 17) |
-                            (static_cast<uint32_t>(BM >> 4) << 24);
+// Instruction descriptors, M = 128, N = 256, D f32, both operands K-major:
+// kind::tf32 (A, B format 2 = TF32) and kind::f16 with bf16 (format 1).
+constexpr uint32_t kIdescShape =
+    (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+constexpr uint32_t kIdescTf32 = (1u << 4) | (2u << 7) | (2u << 10) | kIdescShape;
+constexpr uint32_t kIdescBf16 = (1u << 4) | (1u << 7) | (1u << 10) | kIdescShape;
 
-// Grouped raster: consecutive CTAs walk down kGroupM row-tiles before moving
-// right, so CTAs resident together share A row-blocks and B column-blocks in L2.
+// Grouped raster: consecutive tiles walk down kGroupM row-tiles before moving
+// right, so tiles in flight together share A row-blocks and B column-blocks in L2.
 constexpr int kGroupM = 16;
 __device__ __forceinline__ void tile_coords(int tile, int mt, int nt, int& m_tile, int& n_tile) {
     const int group_size = kGroupM * nt;
@@ -104,12 +121,44 @@ __device__ __forceinline__ void tile_coords(int tile, int mt, int nt, int& m_til
     n_tile = r / gm;
 }
 
-template <int kPlanes>
+// Issues the MMAs of one smem stage into d_tmem; `first` starts a fresh
+// accumulation (the first MMA overwrites D).  Every operand is K-major with
+// 128-byte swizzled rows (SBO = 8 rows = 1024 B); a term is selected by its
+// byte offset inside the row: TF32 k-steps at 32 B apart; TF32X3 hi at +0,
+// lo at +64; TF32_BF16X2 tf32 hi at +0, bf16 hi at +64, bf16 lo at +96.
+template <int S>
+__device__ __forceinline__ void issue_stage(uint32_t d_tmem, uint32_t stage_base, bool first) {
+    using Cfg = TcCfg<S>;
+    const uint32_t a = stage_base, b = stage_base + Cfg::A_BYTES;
+    auto d = [](uint32_t addr) { return umma_desc(addr, 16, 1024, 2); };
+    uint32_t acc = first ? 0u : 1u;
+    if (S == 3) {
+        // bf16 corrections first (small terms into the accumulator first),
+        // one K = 16 MMA each covering the whole stage
+        mma_f16_ss(d_tmem, d(a + 96), d(b + 64), kIdescBf16, acc);
+        acc = 1u;
+        mma_f16_ss(d_tmem, d(a + 64), d(b + 96), kIdescBf16, 1u);
+    }
+#pragma unroll
+    for (int kk = 0; kk < (S == 1 ? 4 : 2); ++kk) {
+        // K = 8 per tf32 MMA: 32 bytes along the swizzled row
+        const uint32_t ko = kk * 32;
+        if (S == 2) {
+            mma_tf32_ss(d_tmem, d(a + 64 + ko), d(b + ko), kIdescTf32, acc);
+            acc = 1u;
+            mma_tf32_ss(d_tmem, d(a + ko), d(b + 64 + ko), kIdescTf32, 1u);
+        }
+        mma_tf32_ss(d_tmem, d(a + ko), d(b + ko), kIdescTf32, acc);
+        acc = 1u;
+    }
+}
+
+template <int S>
 __global__ void __launch_bounds__(kTcThreads, 1)
     sgemm_tc_kernel(const __grid_constant__ TcMaps maps, int M, int N, int K, float alpha,
                     float* __restrict__ C, int64_t ldc, const float* __restrict__ bias, int relu,
                     int vec_c) {
-    using Cfg = TcCfg<kPlanes>;
+    using Cfg = TcCfg<S>;
     constexpr int BK = Cfg::BK, STAGES = Cfg::STAGES;
 
     extern __shared__ uint8_t smem_raw[];
@@ -135,11 +184,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         n0 = ni * BN;
     };
 
-    auto a_plane = [&](int s, int p) { return smem + s * Cfg::STAGE_BYTES + p * Cfg::A_BYTES; };
-    auto b_plane = [&](int s, int p) {
-        return smem + s * Cfg::STAGE_BYTES + kPlanes * Cfg::A_BYTES + p * Cfg::B_BYTES;
-    };
-
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
@@ -153,10 +197,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
-        for (int p = 0; p < kPlanes; ++p) {
-            prefetch_tensormap(&maps.a[p]);
-            prefetch_tensormap(&maps.b[p]);
-        }
+        prefetch_tensormap(&maps.a);
+        prefetch_tensormap(&maps.b);
     }
     if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
     tc_fence_before();
@@ -180,11 +222,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
-                    const int k0 = kb * BK;
-                    for (int p = 0; p < kPlanes; ++p) {
-                        tma_load_2d(a_plane(s, p), &maps.a[p], k0, m0, &full[s]);
-                        tma_load_2d(b_plane(s, p), &maps.b[p], k0, n0, &full[s]);
-                    }
+                    uint8_t* st = smem + s * Cfg::STAGE_BYTES;
+                    // k-block kb is 32 four-byte units into every row (TF32: 32
+                    // f32 of k; split modes: one interleaved 128-byte block)
+                    tma_load_2d(st, &maps.a, kb * 32, m0, &full[s]);
+                    tma_load_2d(st + Cfg::A_BYTES, &maps.b, kb * 32, n0, &full[s]);
                 }
             }
             // Make sure no copy is still landing in shared memory at exit.
@@ -218,30 +260,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t a0 = smem_u32(a_plane(s, 0));
-                        const uint32_t b0 = smem_u32(b_plane(s, 0));
-#pragma unroll
-                        for (int kk = 0; kk < BK / 8; ++kk) {
-                            // Advance 8 f32 (32 bytes) inside the swizzled K row.
-                            const uint64_t ahi =
-                                umma_desc(a0 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
-                            const uint64_t bhi =
-                                umma_desc(b0 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
-                            const uint32_t acc0 = (kb != kb0 || kk != 0) ? 1u : 0u;
-                            if (kPlanes == 2) {
-                                const uint32_t a1 = smem_u32(a_plane(s, 1));
-                                const uint32_t b1 = smem_u32(b_plane(s, 1));
-                                const uint64_t alo =
-                                    umma_desc(a1 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
-                                const uint64_t blo =
-                                    umma_desc(b1 + kk * 32, 16, Cfg::SBO, Cfg::LAYOUT);
-                                mma_tf32_ss(d_tmem, alo, bhi, kIdesc, acc0);
-                                mma_tf32_ss(d_tmem, ahi, blo, kIdesc, 1u);
-                                mma_tf32_ss(d_tmem, ahi, bhi, kIdesc, 1u);
-                            } else {
-                                mma_tf32_ss(d_tmem, ahi, bhi, kIdesc, acc0);
-                            }
-                        }
+                        issue_stage<S>(d_tmem, smem_u32(smem + s * Cfg::STAGE_BYTES), kb == kb0);
                         mma_commit(&empty[s]);  // stage s free once these MMAs finish
                     }
                     if (ok) mma_commit(&acc_full[buf]);  // chunk complete in buffer buf
@@ -254,8 +273,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else {
         // ---------------- epilogue (warps 2..9) ----------------
-        const int q = warp & 3;             // TMEM lane quarter this warp may access
-        const int half = (warp - 2) >> 2;   // 128-column half of the tile
+        const int q = warp & 3;            // TMEM lane quarter this warp may access
+        const int half = (warp - 2) >> 2;  // 128-column half of the tile
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + half * 128;
         bool ok = true;
         int cj = 0;
@@ -322,51 +341,93 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
-// ---- split / pad pre-pass ---------------------------------------------------
-// dst_hi[r, c] = tf32(src[r, c]); dst_lo[r, c] = tf32(src - hi) (when non-null);
-// rows of `cols` elements, source pitch `lds`, destination pitch `ldd`.
-// With dst_lo == null and round == 0 it is a plain pitched copy.
-__global__ void __launch_bounds__(256)
-    split_planes_kernel(const float* __restrict__ src, int rows, int cols, int64_t lds,
-                        float* __restrict__ hi, float* __restrict__ lo, int64_t ldd, int round) {
-    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
-        const float* s = src + r * lds;
-        float* h = hi + r * ldd;
-        float* l = lo ? lo + r * ldd : nullptr;
-        for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-            const float x = __ldcs(s + c);
-            const float xh = round ? to_tf32(x) : x;
-            h[c] = xh;
-            if (l) l[c] = to_tf32(__fsub_rn(x, xh));
-        }
+// ---- operand pre-pass ------------------------------------------------------------
+// Writes element (row r, k) of one operand view.  TF32 (S = 1): f32 copy;
+// TF32X3 (S = 2): block kb = k / 16 holds tf32(x) at [kb*32 + j] and
+// tf32(x - hi) at [kb*32 + 16 + j]; TF32_BF16X2 (S = 3): tf32(x) at
+// [kb*32 + j], then 16 bf16(hi) and 16 bf16(x - hi) in the block's last
+// 64 bytes.  j = k % 16.  x = 0 for padding k, so the padding is zero.
+template <int S>
+__device__ __forceinline__ void put_value(float* base, int64_t ld, int64_t r, int k, float x) {
+    float* row = base + r * ld;
+    if (S == 1) {
+        row[k] = x;
+        return;
+    }
+    const float h = to_tf32(x);
+    const float l = __fsub_rn(x, h);  // exact: h is x with its low mantissa bits rounded off
+    float* blk = row + (k >> 4) * 32;
+    const int j = k & 15;
+    blk[j] = h;
+    if (S == 2) {
+        blk[16 + j] = to_tf32(l);
+    } else {
+        __nv_bfloat16* bb = reinterpret_cast<__nv_bfloat16*>(blk + 16);
+        bb[j] = __float2bfloat16_rn(h);
+        bb[16 + j] = __float2bfloat16_rn(l);
     }
 }
 
-__global__ void __launch_bounds__(256)
-    split_planes_vec_kernel(const float4* __restrict__ src, int rows, int cols4, int64_t lds4,
-                            float4* __restrict__ hi, float4* __restrict__ lo, int64_t ldd4) {
-    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
-        const float4* s = src + r * lds4;
-        float4* h = hi + r * ldd4;
-        float4* l = lo + r * ldd4;
-        for (int c = threadIdx.x; c < cols4; c += blockDim.x) {
-            const float4 x = __ldcs(s + c);
-            const float4 xh = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
-            h[c] = xh;
-            l[c] = make_float4(to_tf32(__fsub_rn(x.x, xh.x)), to_tf32(__fsub_rn(x.y, xh.y)),
-                               to_tf32(__fsub_rn(x.z, xh.z)), to_tf32(__fsub_rn(x.w, xh.w)));
-        }
+// Four consecutive k (k % 4 == 0) of one row with vector stores.
+template <int S>
+__device__ __forceinline__ void put_value4(float* base, int64_t ld, int64_t r, int k, float4 x) {
+    float* row = base + r * ld;
+    if (S == 1) {
+        *reinterpret_cast<float4*>(row + k) = x;
+        return;
+    }
+    const float xs[4] = {x.x, x.y, x.z, x.w};
+    float h[4], l[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        h[u] = to_tf32(xs[u]);
+        l[u] = __fsub_rn(xs[u], h[u]);
+    }
+    float* blk = row + (k >> 4) * 32;
+    const int j = k & 15;
+    *reinterpret_cast<float4*>(blk + j) = make_float4(h[0], h[1], h[2], h[3]);
+    if (S == 2) {
+        *reinterpret_cast<float4*>(blk + 16 + j) =
+            make_float4(to_tf32(l[0]), to_tf32(l[1]), to_tf32(l[2]), to_tf32(l[3]));
+    } else {
+        __nv_bfloat162 bh[2] = {__floats2bfloat162_rn(h[0], h[1]), __floats2bfloat162_rn(h[2], h[3])};
+        __nv_bfloat162 bl[2] = {__floats2bfloat162_rn(l[0], l[1]), __floats2bfloat162_rn(l[2], l[3])};
+        __nv_bfloat16* bb = reinterpret_cast<__nv_bfloat16*>(blk + 16);
+        *reinterpret_cast<uint2*>(bb + j) = *reinterpret_cast<uint2*>(bh);
+        *reinterpret_cast<uint2*>(bb + 16 + j) = *reinterpret_cast<uint2*>(bl);
     }
 }
 
-// Transposing variant for B: dst[n, k] = f(src[k, n]) from a K x N source
-// (pitch lds) into N x K planes (pitch ldd), through a 32 x 33 shared tile so
-// both the reads and the writes are coalesced.  hi = tf32(x) (round) or x;
-// lo = tf32(x - hi) when `lo` is non-null.
+// Row-wise pre-pass: rows x K source (pitch lds) -> view with kpad k per row
+// (kpad a multiple of 4; k >= K written as zero).  blockIdx.y strides rows.
+template <int S>
 __global__ void __launch_bounds__(256)
-    transpose_planes_kernel(const float* __restrict__ src, int K, int N, int64_t lds,
-                            float* __restrict__ hi, float* __restrict__ lo, int64_t ldd,
-                            int round) {
+    prep_rows_kernel(const float* __restrict__ src, int rows, int K, int64_t lds, float* dst,
+                     int64_t ldd, int kpad, int vec) {
+    const int k = (blockIdx.x * 256 + threadIdx.x) * 4;
+    if (k >= kpad) return;
+    for (int r = blockIdx.y; r < rows; r += gridDim.y) {
+        const float* s = src + static_cast<int64_t>(r) * lds;
+        float4 x;
+        if (vec && k + 3 < K) {
+            x = __ldcs(reinterpret_cast<const float4*>(s + k));
+        } else {
+            x.x = k + 0 < K ? s[k + 0] : 0.f;
+            x.y = k + 1 < K ? s[k + 1] : 0.f;
+            x.z = k + 2 < K ? s[k + 2] : 0.f;
+            x.w = k + 3 < K ? s[k + 3] : 0.f;
+        }
+        put_value4<S>(dst, ldd, r, k, x);
+    }
+}
+
+// Transposing pre-pass for B: view row n, k from a K x N source (pitch lds),
+// through a 32 x 33 shared tile so both reads and writes are coalesced;
+// k in [K, kpad) written as zero.
+template <int S>
+__global__ void __launch_bounds__(256)
+    prep_transpose_kernel(const float* __restrict__ src, int K, int N, int64_t lds, float* dst,
+                          int64_t ldd, int kpad) {
     __shared__ float tile[32][33];
     const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
@@ -379,25 +440,29 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int j = ty; j < 32; j += 8) {
         const int n = n0 + j, k = k0 + tx;
-        if (n < N && k < K) {
-            const float x = tile[tx][j];
-            const float h = round ? to_tf32(x) : x;
-            const int64_t o = static_cast<int64_t>(n) * ldd + k;
-            hi[o] = h;
-            if (lo) lo[o] = to_tf32(__fsub_rn(x, h));
-        }
+        if (n < N && k < kpad) put_value<S>(dst, ldd, n, k, tile[tx][j]);
     }
 }
 
+// Plain pitched copy (SIMT packing of B).
+__global__ void __launch_bounds__(256)
+    copy_rows_kernel(const float* __restrict__ src, int rows, int cols, int64_t lds,
+                     float* __restrict__ dst, int64_t ldd) {
+    for (int r = blockIdx.x; r < rows; r += gridDim.x)
+        for (int c = threadIdx.x; c < cols; c += blockDim.x) dst[r * ldd + c] = src[r * lds + c];
+}
+
 // C = epilogue(alpha * 0) for K == 0 (an empty sum, as the reference loop).
-__global__ void gemm_k0_kernel(int M, int N, float alpha, float* C, const float* bias, int relu) {
+__global__ void gemm_k0_kernel(int M, int N, float alpha, float* C, int64_t ldc,
+                               const float* bias, int relu) {
     const int64_t total = static_cast<int64_t>(M) * N;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / N, c = i - r * N;
         float x = __fmul_rn(alpha, 0.0f);
-        if (bias) x = __fadd_rn(x, bias[i % N]);
+        if (bias) x = __fadd_rn(x, bias[c]);
         if (relu) x = relu1(x);
-        C[i] = x;
+        C[r * ldc + c] = x;
     }
 }
 
@@ -416,18 +481,27 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     return fn;
 }
 
-// 2-D row-major f32 map: inner extent `cols`, outer `rows`, pitch `ld`
-// elements, box {box_x, box_y}.
-int encode_map(CUtensorMap* map, const float* base, uint64_t cols, uint64_t rows, uint64_t ld,
-               uint32_t box_x, uint32_t box_y, CUtensorMapSwizzle swz) {
+uint64_t round_up(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+int sm_count() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms > 0 ? sms : 148;
+}
+
+// 2-D map over `rows` rows of `cols` 4-byte units, pitch `ld` units, box
+// {32 units (128 B), box_rows}, 128-byte swizzle.
+int encode_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld,
+               uint32_t box_rows) {
     auto fn = get_encode_fn();
     if (!fn) return set_error(ZG_ERR_BACKEND, "cuTensorMapEncodeTiled unavailable");
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {ld * 4};
-    cuuint32_t box[2] = {box_x, box_y};
+    cuuint32_t box[2] = {32, box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
-                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return set_error(ZG_ERR_BACKEND, "cuTensorMapEncodeTiled failed (%d): %llux%llu ld=%llu",
@@ -436,78 +510,75 @@ int encode_map(CUtensorMap* map, const float* base, uint64_t cols, uint64_t rows
     return ZG_OK;
 }
 
-uint64_t round_up(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-struct WsLayout {
-    uint64_t a_hi, a_lo, b_hi, b_lo, total;  // byte offsets; ~0 = unused
-};
-
-constexpr uint64_t kNone = ~0ull;
-
-WsLayout ws_layout(int mode, int m, int n, int k) {
-    WsLayout w{kNone, kNone, kNone, kNone, 0};
-    // A planes M x kp, B planes (transposed, K-major) N x kp.
-    const uint64_t kp = round_up(k, 4);
-    const uint64_t a_bytes = round_up(static_cast<uint64_t>(m) * kp * 4, 256);
-    const uint64_t b_bytes = round_up(static_cast<uint64_t>(n) * kp * 4, 256);
-    uint64_t off = 0;
-    if (mode == ZG_GEMM_TF32X3) {
-        w.a_hi = off; off += a_bytes;
-        w.a_lo = off; off += a_bytes;
-        w.b_hi = off; off += b_bytes;
-        w.b_lo = off; off += b_bytes;
-    } else if (mode == ZG_GEMM_TF32) {
-        if (k % 4 != 0) { w.a_hi = off; off += a_bytes; }
-        w.b_hi = off; off += b_bytes;
-    }
-    w.total = off;
-    return w;
-}
-
-unsigned split_grid(int rows) {
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int cap = sms * 8;
+unsigned row_grid(int rows) {
+    const int cap = sm_count() * 8;
     return static_cast<unsigned>(rows < cap ? (rows < 1 ? 1 : rows) : cap);
 }
 
-// Writes the tf32 hi (and lo) planes of a rows x cols matrix into pitch-ldd
-// buffers; a plain pitched copy when lo == null and round == 0.
-int launch_split(const float* src, int rows, int cols, int64_t lds, float* hi, float* lo,
-                 int64_t ldd, int round, cudaStream_t s) {
-    if (rows == 0 || cols == 0) return ZG_OK;
-    if (lo && round && cols % 4 == 0 && lds % 4 == 0 && ldd % 4 == 0 && aligned16(src) &&
-        aligned16(hi) && aligned16(lo)) {
-        split_planes_vec_kernel<<<split_grid(rows), 256, 0, s>>>(
-            reinterpret_cast<const float4*>(src), rows, cols / 4, lds / 4,
-            reinterpret_cast<float4*>(hi), reinterpret_cast<float4*>(lo), ldd / 4);
-    } else {
-        split_planes_kernel<<<split_grid(rows), 256, 0, s>>>(src, rows, cols, lds, hi, lo, ldd,
-                                                             round);
+bool valid_mode(int mode) {
+    return mode == ZG_GEMM_SIMT_FP32 || mode == ZG_GEMM_TF32X3 || mode == ZG_GEMM_TF32 ||
+           mode == ZG_GEMM_TF32_BF16X2;
+}
+
+// Kernel scheme of a tensor-core mode (0: SIMT).
+int scheme_of(int mode) {
+    return mode == ZG_GEMM_TF32 ? 1 : mode == ZG_GEMM_TF32X3 ? 2
+                                  : mode == ZG_GEMM_TF32_BF16X2 ? 3 : 0;
+}
+
+// k values stored per row of a prepared operand and its pitch (4-byte units).
+int64_t view_kpad(int mode, int K) {
+    return scheme_of(mode) == 1 ? static_cast<int64_t>(round_up(K, 4))
+                                : static_cast<int64_t>(round_up(K, 16));
+}
+int64_t view_pitch(int mode, int K) {
+    return scheme_of(mode) == 1 ? view_kpad(mode, K) : view_kpad(mode, K) * 2;
+}
+// 4-byte units of the global inner dimension the tensor map covers.
+uint64_t map_cols(int mode, int K) {
+    return scheme_of(mode) == 1 ? static_cast<uint64_t>(K) : static_cast<uint64_t>(view_pitch(mode, K));
+}
+
+int launch_prep_rows(int mode, const float* src, int rows, int K, int64_t lds,
+                     const OperandView& v, cudaStream_t s) {
+    if (rows == 0 || K == 0) return ZG_OK;
+    const int kpad = static_cast<int>(view_kpad(mode, K));
+    const int vec = lds % 4 == 0 && aligned16(src);
+    dim3 grid((kpad / 4 + 255) / 256, static_cast<unsigned>(std::min(rows, 65535)));
+    float* dst = static_cast<float*>(v.p);
+    switch (scheme_of(mode)) {
+        case 1: prep_rows_kernel<1><<<grid, 256, 0, s>>>(src, rows, K, lds, dst, v.ld, kpad, vec); break;
+        case 2: prep_rows_kernel<2><<<grid, 256, 0, s>>>(src, rows, K, lds, dst, v.ld, kpad, vec); break;
+        case 3: prep_rows_kernel<3><<<grid, 256, 0, s>>>(src, rows, K, lds, dst, v.ld, kpad, vec); break;
+        default: return set_error(ZG_ERR_DISPATCH, "sgemm pre-pass: no planes for mode %d", mode);
     }
     return cuda_status(cudaGetLastError(), "sgemm split pre-pass");
 }
 
-// Writes the K-major (transposed) planes of B: N x K, pitch ldd.
-int launch_transpose(const float* src, int K, int N, int64_t lds, float* hi, float* lo,
-                     int64_t ldd, int round, cudaStream_t s) {
+int launch_prep_transpose(int mode, const float* src, int K, int N, int64_t lds,
+                          const OperandView& v, cudaStream_t s) {
     if (K == 0 || N == 0) return ZG_OK;
-    dim3 grid((N + 31) / 32, (K + 31) / 32);
+    const int kpad = static_cast<int>(view_kpad(mode, K));
+    dim3 grid((N + 31) / 32, (kpad + 31) / 32);
     if (grid.y > 65535u) return set_error(ZG_ERR_DISPATCH, "sgemm: k too large for the pre-pass");
-    transpose_planes_kernel<<<grid, 256, 0, s>>>(src, K, N, lds, hi, lo, ldd, round);
+    float* dst = static_cast<float*>(v.p);
+    switch (scheme_of(mode)) {
+        case 1: prep_transpose_kernel<1><<<grid, 256, 0, s>>>(src, K, N, lds, dst, v.ld, kpad); break;
+        case 2: prep_transpose_kernel<2><<<grid, 256, 0, s>>>(src, K, N, lds, dst, v.ld, kpad); break;
+        case 3: prep_transpose_kernel<3><<<grid, 256, 0, s>>>(src, K, N, lds, dst, v.ld, kpad); break;
+        default: return set_error(ZG_ERR_DISPATCH, "sgemm pre-pass: no planes for mode %d", mode);
+    }
     return cuda_status(cudaGetLastError(), "sgemm transpose pre-pass");
 }
 
-template <int kPlanes>
+template <int S>
 int launch_tc(const TcMaps& maps, int M, int N, int K, float alpha, float* C, int64_t ldc,
               const float* bias, int relu, cudaStream_t s) {
-    using Cfg = TcCfg<kPlanes>;
+    using Cfg = TcCfg<S>;
     static std::once_flag attr_once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(attr_once, [] {
-        attr_err = cudaFuncSetAttribute(sgemm_tc_kernel<kPlanes>,
+        attr_err = cudaFuncSetAttribute(sgemm_tc_kernel<S>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         Cfg::SMEM_BYTES);
     });
@@ -515,118 +586,126 @@ int launch_tc(const TcMaps& maps, int M, int N, int K, float alpha, float* C, in
     const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
     const int vec_c = (ldc % 4 == 0) && aligned16(C);
     // Persistent grid: one CTA per SM (the smem footprint allows no more).
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int grid = std::min(mt * nt, std::max(sms, 1));
-    sgemm_tc_kernel<kPlanes><<<grid, kTcThreads, Cfg::SMEM_BYTES, s>>>(maps, M, N, K, alpha, C,
-                                                                      ldc, bias, relu, vec_c);
+    const int grid = std::min(mt * nt, sm_count());
+    sgemm_tc_kernel<S><<<grid, kTcThreads, Cfg::SMEM_BYTES, s>>>(maps, M, N, K, alpha, C, ldc,
+                                                                bias, relu, vec_c);
     return cuda_status(cudaGetLastError(), "sgemm_tc");
+}
+
+template <int S>
+int run_tc(const GemmOperands& op, int M, int N, int K, float alpha, float* C, int64_t ldc,
+           const float* bias, int relu, cudaStream_t s) {
+    for (const OperandView* v : {&op.a, &op.b})
+        if (!v->p || !aligned16(v->p) || v->ld % 4 != 0)
+            return set_error(ZG_ERR_DISPATCH,
+                             "sgemm (tensor-core mode): operands must be 16-byte aligned with a "
+                             "pitch of a multiple of 16 bytes");
+    TcMaps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    const uint64_t cols = map_cols(op.mode, K);
+    // TF32's A may be the caller's operand: its map covers exactly K columns
+    const uint64_t acols = S == 1 ? static_cast<uint64_t>(K) : cols;
+    int rc = encode_map(&maps.a, op.a.p, acols, M, op.a.ld, BM);
+    if (!rc) rc = encode_map(&maps.b, op.b.p, cols, N, op.b.ld, BN);
+    if (rc) return rc;
+    return launch_tc<S>(maps, M, N, K, alpha, C, ldc, bias, relu, s);
 }
 
 }  // namespace
 
-// ---- GEMM building blocks (shared with the runtime's pipelined host GEMM) ----
+// ---- GEMM building blocks (shared with the packed API and the host GEMM) -----------
 bool gemm_a_needs_planes(int mode, int K) {
-    return mode == ZG_GEMM_TF32X3 || (mode == ZG_GEMM_TF32 && K % 4 != 0);
+    return mode == ZG_GEMM_TF32X3 || mode == ZG_GEMM_TF32_BF16X2 ||
+           (mode == ZG_GEMM_TF32 && K % 4 != 0);
 }
-bool gemm_b_needs_planes(int mode) { return mode == ZG_GEMM_TF32X3 || mode == ZG_GEMM_TF32; }
-int64_t gemm_plane_pitch(int K) { return static_cast<int64_t>(round_up(K, 4)); }
+bool gemm_b_needs_planes(int mode) { return scheme_of(mode) > 0; }
 
-int gemm_prep_a(int mode, int M, int K, const float* A, int64_t lda, float* hi, float* lo,
-                int64_t ldp, cudaStream_t s) {
-    if (mode == ZG_GEMM_TF32X3) return launch_split(A, M, K, lda, hi, lo, ldp, 1, s);
-    if (mode == ZG_GEMM_TF32 && K % 4 != 0)
-        return launch_split(A, M, K, lda, hi, nullptr, ldp, 0, s);
-    return ZG_OK;
+uint64_t gemm_planes_bytes(int mode, int outer, int K) {
+    if (scheme_of(mode) == 0 || outer <= 0 || K <= 0) return 0;
+    return round_up(static_cast<uint64_t>(outer) * view_pitch(mode, K) * 4, 256);
 }
 
-int gemm_prep_b(int mode, int K, int N, const float* B, int64_t ldb, float* hi, float* lo,
-                int64_t ldp, cudaStream_t s) {
-    if (mode == ZG_GEMM_TF32X3) return launch_transpose(B, K, N, ldb, hi, lo, ldp, 1, s);
-    if (mode == ZG_GEMM_TF32) return launch_transpose(B, K, N, ldb, hi, nullptr, ldp, 0, s);
-    return ZG_OK;
+OperandView gemm_carve_planes(void* base, int mode, int outer, int K) {
+    (void)outer;
+    OperandView v;
+    v.p = base;
+    v.ld = view_pitch(mode, K);
+    return v;
+}
+
+OperandView gemm_offset_rows(const OperandView& v, int64_t rows) {
+    OperandView o = v;
+    o.p = static_cast<float*>(v.p) + rows * v.ld;
+    return o;
+}
+
+OperandView gemm_raw_operand(const float* x, int64_t ld) {
+    OperandView v;
+    v.p = const_cast<float*>(x);
+    v.ld = ld;
+    return v;
+}
+
+int gemm_prep_a(int mode, int M, int K, const float* A, int64_t lda, const OperandView& out,
+                cudaStream_t s) {
+    if (!gemm_a_needs_planes(mode, K)) return ZG_OK;
+    return launch_prep_rows(mode, A, M, K, lda, out, s);
+}
+
+int gemm_prep_b(int mode, int K, int N, const float* B, int64_t ldb, const OperandView& out,
+                cudaStream_t s) {
+    if (!gemm_b_needs_planes(mode)) return ZG_OK;
+    return launch_prep_transpose(mode, B, K, N, ldb, out, s);
 }
 
 int gemm_run(const GemmOperands& op, int M, int N, int K, float alpha, float* C, int64_t ldc,
              const float* bias, int relu, cudaStream_t s) {
-    if (op.mode == ZG_GEMM_SIMT_FP32)
-        return launch_sgemm_simt(M, N, K, alpha, op.a_hi, op.lda, op.b_hi, op.ldb, C, ldc, bias,
-                                 relu, s);
-    TcMaps maps;
-    std::memset(&maps, 0, sizeof(maps));
-    int rc;
-    if (!aligned16(op.a_hi) || !aligned16(op.b_hi) || op.lda % 4 != 0 || op.ldb % 4 != 0)
-        return set_error(ZG_ERR_DISPATCH,
-                         "sgemm (tensor-core mode): operand planes must be 16-byte aligned with a "
-                         "pitch that is a multiple of 4 floats");
-    if (op.mode == ZG_GEMM_TF32X3) {
-        using Cfg = TcCfg<2>;
-        const CUtensorMapSwizzle swz =
-            Cfg::BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-        if ((rc = encode_map(&maps.a[0], op.a_hi, K, M, op.lda, Cfg::BK, BM, swz))) return rc;
-        if ((rc = encode_map(&maps.a[1], op.a_lo, K, M, op.lda, Cfg::BK, BM, swz))) return rc;
-        if ((rc = encode_map(&maps.b[0], op.b_hi, K, N, op.ldb, Cfg::BK, BN, swz))) return rc;
-        if ((rc = encode_map(&maps.b[1], op.b_lo, K, N, op.ldb, Cfg::BK, BN, swz))) return rc;
-        return launch_tc<2>(maps, M, N, K, alpha, C, ldc, bias, relu, s);
+    switch (op.mode) {
+        case ZG_GEMM_SIMT_FP32:
+            return launch_sgemm_simt(M, N, K, alpha, static_cast<const float*>(op.a.p), op.a.ld,
+                                     static_cast<const float*>(op.b.p), op.b.ld, C, ldc, bias,
+                                     relu, s);
+        case ZG_GEMM_TF32: return run_tc<1>(op, M, N, K, alpha, C, ldc, bias, relu, s);
+        case ZG_GEMM_TF32X3: return run_tc<2>(op, M, N, K, alpha, C, ldc, bias, relu, s);
+        case ZG_GEMM_TF32_BF16X2: return run_tc<3>(op, M, N, K, alpha, C, ldc, bias, relu, s);
+        default: return set_error(ZG_ERR_DISPATCH, "sgemm: unknown mode %d", op.mode);
     }
-    using Cfg = TcCfg<1>;
-    if ((rc = encode_map(&maps.a[0], op.a_hi, K, M, op.lda, Cfg::BK, BM,
-                         CU_TENSOR_MAP_SWIZZLE_128B)))
-        return rc;
-    if ((rc = encode_map(&maps.b[0], op.b_hi, K, N, op.ldb, Cfg::BK, BN,
-                         CU_TENSOR_MAP_SWIZZLE_128B)))
-        return rc;
-    return launch_tc<1>(maps, M, N, K, alpha, C, ldc, bias, relu, s);
 }
 
 namespace {
 
-// The operands zg_sgemm_compute reads for (mode, m, n, k) in workspace `ws`.
+// Workspace of zg_sgemm_f32 / prepare / compute: A's prepared form, then B's.
+struct WsLayout {
+    uint64_t b_off, total;
+    bool a_planes, b_planes;
+};
+
+WsLayout ws_layout(int mode, int m, int n, int k) {
+    WsLayout w{0, 0, false, false};
+    if (m <= 0 || n <= 0 || k <= 0 || !valid_mode(mode)) return w;
+    w.a_planes = gemm_a_needs_planes(mode, k);
+    w.b_planes = gemm_b_needs_planes(mode);
+    w.b_off = w.a_planes ? gemm_planes_bytes(mode, m, k) : 0;
+    w.total = w.b_off + (w.b_planes ? gemm_planes_bytes(mode, n, k) : 0);
+    return w;
+}
+
 GemmOperands operands_in_workspace(int mode, int M, int N, int K, const float* A,
-                                   const float* B, const uint8_t* ws) {
+                                   const float* B, uint8_t* ws) {
     const WsLayout w = ws_layout(mode, M, N, K);
-    const int64_t kp = gemm_plane_pitch(K);
-    auto plane = [&](uint64_t off) {
-        return off == kNone ? nullptr : reinterpret_cast<const float*>(ws + off);
-    };
-    GemmOperands op{mode, A, nullptr, K, B, nullptr, N};
-    if (mode == ZG_GEMM_SIMT_FP32) return op;
-    if (w.a_hi != kNone) {
-        op.a_hi = plane(w.a_hi);
-        op.a_lo = plane(w.a_lo);
-        op.lda = kp;
-    }
-    op.b_hi = plane(w.b_hi);
-    op.b_lo = plane(w.b_lo);
-    op.ldb = kp;
+    GemmOperands op{mode, gemm_raw_operand(A, K), gemm_raw_operand(B, N)};
+    if (w.a_planes) op.a = gemm_carve_planes(ws, mode, M, K);
+    if (w.b_planes) op.b = gemm_carve_planes(ws + w.b_off, mode, N, K);
     return op;
 }
 
-int prepare_planes(int mode, int M, int N, int K, const float* A, const float* B, uint8_t* ws,
-                   cudaStream_t s) {
-    const WsLayout w = ws_layout(mode, M, N, K);
-    const int64_t kp = gemm_plane_pitch(K);
-    auto plane = [&](uint64_t off) {
-        return off == kNone ? nullptr : reinterpret_cast<float*>(ws + off);
-    };
-    int rc = ZG_OK;
-    if (gemm_a_needs_planes(mode, K) &&
-        (rc = gemm_prep_a(mode, M, K, A, K, plane(w.a_hi), plane(w.a_lo), kp, s)) != ZG_OK)
-        return rc;
-    if (gemm_b_needs_planes(mode))
-        rc = gemm_prep_b(mode, K, N, B, N, plane(w.b_hi), plane(w.b_lo), kp, s);
-    return rc;
-}
-
-// Shared argument checks of the three GEMM entry points.  Returns ZG_OK and
+// Shared argument checks of the workspace entry points.  Returns ZG_OK and
 // sets *trivial when there is nothing (m or n is 0) to compute.
 int check_gemm_args(int mode, int m, int n, int k, const float* a, const float* b,
                     const void* workspace, uint64_t workspace_bytes, bool need_c, const float* c,
                     bool* trivial) {
     *trivial = false;
-    if (mode != ZG_GEMM_SIMT_FP32 && mode != ZG_GEMM_TF32X3 && mode != ZG_GEMM_TF32)
-        return set_error(ZG_ERR_DISPATCH, "sgemm: unknown mode %d", mode);
+    if (!valid_mode(mode)) return set_error(ZG_ERR_DISPATCH, "sgemm: unknown mode %d", mode);
     if (m < 0 || n < 0 || k < 0)
         return set_error(ZG_ERR_DISPATCH, "sgemm: negative shape %d x %d x %d", m, n, k);
     if (m == 0 || n == 0) {
@@ -635,7 +714,7 @@ int check_gemm_args(int mode, int m, int n, int k, const float* a, const float* 
     }
     if ((need_c && !c) || (k > 0 && (!a || !b)))
         return set_error(ZG_ERR_DISPATCH, "sgemm: null operand pointer");
-    const uint64_t need = k > 0 ? ws_layout(mode, m, n, k).total : 0;
+    const uint64_t need = ws_layout(mode, m, n, k).total;
     if (need > 0 && (!workspace || workspace_bytes < need))
         return set_error(ZG_ERR_DISPATCH,
                          "sgemm: workspace of %llu bytes needed for %d x %d x %d, got %llu",
@@ -645,13 +724,47 @@ int check_gemm_args(int mode, int m, int n, int k, const float* a, const float* 
     return ZG_OK;
 }
 
+int launch_k0(int m, int n, float alpha, float* c, int64_t ldc, const float* bias, int relu,
+              cudaStream_t s) {
+    gemm_k0_kernel<<<row_grid(m), 256, 0, s>>>(m, n, alpha, c, ldc, bias, relu);
+    return cuda_status(cudaGetLastError(), "sgemm k=0");
+}
+
+// ---- packed operands ----------------------------------------------------------
+// A packed operand holds exactly what the mode's kernel reads (OperandView);
+// for SIMT, A is an f32 copy with pitch round_up(k, 4) and B an f32 copy of
+// its k rows with pitch round_up(n, 4); TF32's A is an f32 copy.
+uint64_t simt_packed_bytes(int operand, int outer, int k) {
+    return operand == 0 ? round_up(static_cast<uint64_t>(outer) * round_up(k, 4) * 4, 256)
+                        : round_up(static_cast<uint64_t>(k) * round_up(outer, 4) * 4, 256);
+}
+
+OperandView packed_view(int mode, int operand, const void* packed, int outer, int k) {
+    if (mode == ZG_GEMM_SIMT_FP32)
+        return gemm_raw_operand(static_cast<const float*>(packed),
+                                static_cast<int64_t>(round_up(operand == 0 ? k : outer, 4)));
+    return gemm_carve_planes(const_cast<void*>(packed), mode, outer, k);
+}
+
+int check_pack(int mode, int outer, int k, int64_t ld, int64_t min_ld, const float* src,
+               void* packed, uint64_t bytes, uint64_t need, const char* what) {
+    if (!valid_mode(mode)) return set_error(ZG_ERR_DISPATCH, "sgemm pack: unknown mode %d", mode);
+    if (outer < 0 || k < 0 || ld < min_ld)
+        return set_error(ZG_ERR_DISPATCH, "sgemm %s: bad shape", what);
+    if (outer == 0 || k == 0) return ZG_OK;
+    if (!src || !packed || bytes < need || (reinterpret_cast<uintptr_t>(packed) & 255u))
+        return set_error(ZG_ERR_DISPATCH,
+                         "sgemm %s: needs a 256-byte aligned buffer of %llu bytes", what,
+                         (unsigned long long)need);
+    return ZG_OK;
+}
+
 }  // namespace
 }  // namespace zg
 
 using namespace zg;
 
 extern "C" uint64_t zg_sgemm_workspace_bytes(int mode, int m, int n, int k) {
-    if (m <= 0 || n <= 0 || k <= 0) return 0;
     return ws_layout(mode, m, n, k).total;
 }
 
@@ -660,9 +773,12 @@ extern "C" int zg_sgemm_prepare(int mode, int m, int n, int k, const float* a, c
     bool trivial;
     int rc = check_gemm_args(mode, m, n, k, a, b, workspace, workspace_bytes, false, nullptr,
                              &trivial);
-    if (rc || trivial || k == 0 || mode == ZG_GEMM_SIMT_FP32) return rc;
-    return prepare_planes(mode, m, n, k, a, b, static_cast<uint8_t*>(workspace),
-                          static_cast<cudaStream_t>(stream));
+    if (rc || trivial || k == 0) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const GemmOperands op =
+        operands_in_workspace(mode, m, n, k, a, b, static_cast<uint8_t*>(workspace));
+    if ((rc = gemm_prep_a(mode, m, k, a, k, op.a, s))) return rc;
+    return gemm_prep_b(mode, k, n, b, n, op.b, s);
 }
 
 extern "C" int zg_sgemm_compute(int mode, int m, int n, int k, float alpha, const float* a,
@@ -672,12 +788,9 @@ extern "C" int zg_sgemm_compute(int mode, int m, int n, int k, float alpha, cons
     int rc = check_gemm_args(mode, m, n, k, a, b, workspace, workspace_bytes, true, c, &trivial);
     if (rc || trivial) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (k == 0) {
-        gemm_k0_kernel<<<split_grid(m), 256, 0, s>>>(m, n, alpha, c, bias, relu);
-        return cuda_status(cudaGetLastError(), "sgemm k=0");
-    }
-    const GemmOperands op =
-        operands_in_workspace(mode, m, n, k, a, b, static_cast<const uint8_t*>(workspace));
+    if (k == 0) return launch_k0(m, n, alpha, c, n, bias, relu, s);
+    const GemmOperands op = operands_in_workspace(
+        mode, m, n, k, a, b, static_cast<uint8_t*>(const_cast<void*>(workspace)));
     return gemm_run(op, m, n, k, alpha, c, n, bias, relu, s);
 }
 
@@ -690,69 +803,35 @@ extern "C" int zg_sgemm_f32(int mode, int m, int n, int k, float alpha, const fl
                             workspace_bytes, stream);
 }
 
-// ---- packed operands ----------------------------------------------------------
-// A packed operand is the plane(s) the GEMM kernel of `mode` reads, each
-// 256-byte aligned, row pitch kp = k rounded up to 4 floats:
-//   A (m x k):  TF32X3 hi, lo;  TF32 one f32 copy;  SIMT one f32 copy.
-//   B (k x n):  TF32X3 B^T hi, lo (n x kp, K-major);  TF32 B^T;  SIMT B itself
-//               (k rows, pitch round_up(n, 4)).
-namespace zg {
-namespace {
-uint64_t packed_plane_bytes(int mode, int operand, int outer, int k) {
-    if (mode == ZG_GEMM_SIMT_FP32 && operand == 1)
-        return round_up(static_cast<uint64_t>(k) * round_up(outer, 4) * 4, 256);
-    return round_up(static_cast<uint64_t>(outer) * round_up(k, 4) * 4, 256);
-}
-int packed_planes(int mode) { return mode == ZG_GEMM_TF32X3 ? 2 : 1; }
-bool valid_mode(int mode) {
-    return mode == ZG_GEMM_SIMT_FP32 || mode == ZG_GEMM_TF32X3 || mode == ZG_GEMM_TF32;
-}
-}  // namespace
-}  // namespace zg
-
 extern "C" uint64_t zg_sgemm_pack_bytes(int mode, int operand, int outer, int k) {
     if (!valid_mode(mode) || (operand != 0 && operand != 1) || outer <= 0 || k <= 0) return 0;
-    return packed_planes(mode) * packed_plane_bytes(mode, operand, outer, k);
+    if (mode == ZG_GEMM_SIMT_FP32) return simt_packed_bytes(operand, outer, k);
+    return gemm_planes_bytes(mode, outer, k);
 }
 
 extern "C" int zg_sgemm_pack_a(int mode, int m, int k, const float* a, int64_t lda, void* packed,
                                uint64_t packed_bytes, void* stream) {
-    if (!valid_mode(mode)) return set_error(ZG_ERR_DISPATCH, "sgemm pack: unknown mode %d", mode);
-    if (m < 0 || k < 0 || lda < k) return set_error(ZG_ERR_DISPATCH, "sgemm pack_a: bad shape");
-    if (m == 0 || k == 0) return ZG_OK;
-    const uint64_t need = zg_sgemm_pack_bytes(mode, 0, m, k);
-    if (!a || !packed || packed_bytes < need || (reinterpret_cast<uintptr_t>(packed) & 255u))
-        return set_error(ZG_ERR_DISPATCH,
-                         "sgemm pack_a: needs a 256-byte aligned buffer of %llu bytes",
-                         (unsigned long long)need);
-    float* hi = static_cast<float*>(packed);
-    float* lo = mode == ZG_GEMM_TF32X3
-                    ? reinterpret_cast<float*>(static_cast<uint8_t*>(packed) +
-                                               packed_plane_bytes(mode, 0, m, k))
-                    : nullptr;
-    return launch_split(a, m, k, lda, hi, lo, gemm_plane_pitch(k), mode == ZG_GEMM_TF32X3 ? 1 : 0,
-                        static_cast<cudaStream_t>(stream));
+    int rc = check_pack(mode, m, k, lda, k, a, packed, packed_bytes,
+                        zg_sgemm_pack_bytes(mode, 0, m, k), "pack_a");
+    if (rc || m == 0 || k == 0) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const OperandView v = packed_view(mode, 0, packed, m, k);
+    // SIMT and TF32 store an f32 copy (the TF32 row pre-pass writes exactly that)
+    return launch_prep_rows(mode == ZG_GEMM_SIMT_FP32 ? ZG_GEMM_TF32 : mode, a, m, k, lda, v, s);
 }
 
 extern "C" int zg_sgemm_pack_b(int mode, int k, int n, const float* b, int64_t ldb, void* packed,
                                uint64_t packed_bytes, void* stream) {
-    if (!valid_mode(mode)) return set_error(ZG_ERR_DISPATCH, "sgemm pack: unknown mode %d", mode);
-    if (n < 0 || k < 0 || ldb < n) return set_error(ZG_ERR_DISPATCH, "sgemm pack_b: bad shape");
-    if (n == 0 || k == 0) return ZG_OK;
-    const uint64_t need = zg_sgemm_pack_bytes(mode, 1, n, k);
-    if (!b || !packed || packed_bytes < need || (reinterpret_cast<uintptr_t>(packed) & 255u))
-        return set_error(ZG_ERR_DISPATCH,
-                         "sgemm pack_b: needs a 256-byte aligned buffer of %llu bytes",
-                         (unsigned long long)need);
+    int rc = check_pack(mode, n, k, ldb, n, b, packed, packed_bytes,
+                        zg_sgemm_pack_bytes(mode, 1, n, k), "pack_b");
+    if (rc || n == 0 || k == 0) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    float* hi = static_cast<float*>(packed);
-    if (mode == ZG_GEMM_SIMT_FP32)
-        return launch_split(b, k, n, ldb, hi, nullptr, static_cast<int64_t>(round_up(n, 4)), 0, s);
-    float* lo = mode == ZG_GEMM_TF32X3
-                    ? reinterpret_cast<float*>(static_cast<uint8_t*>(packed) +
-                                               packed_plane_bytes(mode, 1, n, k))
-                    : nullptr;
-    return gemm_prep_b(mode, k, n, b, ldb, hi, lo, gemm_plane_pitch(k), s);
+    const OperandView v = packed_view(mode, 1, packed, n, k);
+    if (mode == ZG_GEMM_SIMT_FP32) {
+        copy_rows_kernel<<<row_grid(k), 256, 0, s>>>(b, k, n, ldb, static_cast<float*>(v.p), v.ld);
+        return cuda_status(cudaGetLastError(), "sgemm pack_b");
+    }
+    return launch_prep_transpose(mode, b, k, n, ldb, v, s);
 }
 
 extern "C" int zg_sgemm_packed(int mode, int m, int n, int k, float alpha, const void* a_packed,
@@ -763,23 +842,12 @@ extern "C" int zg_sgemm_packed(int mode, int m, int n, int k, float alpha, const
         return set_error(ZG_ERR_DISPATCH, "sgemm_packed: bad shape %d x %d x %d, ldc %lld", m, n,
                          k, (long long)ldc);
     if (m == 0 || n == 0) return ZG_OK;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (!c) return set_error(ZG_ERR_DISPATCH, "sgemm_packed: null C");
-    if (k == 0) {
-        if (ldc != n) return set_error(ZG_ERR_DISPATCH, "sgemm_packed: k = 0 needs ldc = n");
-        gemm_k0_kernel<<<split_grid(m), 256, 0, s>>>(m, n, alpha, c, bias, relu);
-        return cuda_status(cudaGetLastError(), "sgemm k=0");
-    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (k == 0) return launch_k0(m, n, alpha, c, ldc, bias, relu, s);
     if (!a_packed || !b_packed) return set_error(ZG_ERR_DISPATCH, "sgemm_packed: null operand");
-    const uint8_t* pa = static_cast<const uint8_t*>(a_packed);
-    const uint8_t* pb = static_cast<const uint8_t*>(b_packed);
-    GemmOperands op{mode, reinterpret_cast<const float*>(pa), nullptr, gemm_plane_pitch(k),
-                    reinterpret_cast<const float*>(pb), nullptr, gemm_plane_pitch(k)};
-    if (mode == ZG_GEMM_TF32X3) {
-        op.a_lo = reinterpret_cast<const float*>(pa + packed_plane_bytes(mode, 0, m, k));
-        op.b_lo = reinterpret_cast<const float*>(pb + packed_plane_bytes(mode, 1, n, k));
-    }
-    if (mode == ZG_GEMM_SIMT_FP32) op.ldb = static_cast<int64_t>(round_up(n, 4));
+    const GemmOperands op{mode, packed_view(mode, 0, a_packed, m, k),
+                          packed_view(mode, 1, b_packed, n, k)};
     return gemm_run(op, m, n, k, alpha, c, ldc, bias, relu, s);
 }
 

@@ -1,7 +1,8 @@
 // zg_gemm_internal.h - host-side GEMM building blocks shared inside the
-// library (not exported): the operand pre-pass for A and for B, and the GEMM
-// kernel launch on prepared operands with a pitched C.  zg_sgemm_* and the
-// runtime's pipelined host-buffer GEMM are built from these.
+// library (not exported): the packed operand layout the tensor-core kernels
+// read, the pre-pass that writes it, and the GEMM launch on prepared operands
+// with a pitched C.  zg_sgemm_*, the packed-operand API and the runtime's
+// pipelined host-buffer GEMM are built from these.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -10,31 +11,44 @@
 
 namespace zg {
 
-// What the GEMM kernels read.  SIMT: a_hi = A (M x K, pitch lda), b_hi = B
-// (K x N row-major, pitch ldb).  Tensor-core modes: A or its tf32 planes
-// (M x K, K-major) and the K-major planes of B^T (N x K), pitches in floats.
-struct GemmOperands {
-    int mode;
-    const float* a_hi;
-    const float* a_lo;
-    int64_t lda;
-    const float* b_hi;
-    const float* b_lo;
-    int64_t ldb;
+// One operand as a kernel reads it: `rows` rows (A: m; B: n, i.e. B
+// transposed so k is innermost), pitch `ld` in 4-byte units.
+//   SIMT          the caller's f32 operand (B untransposed: k rows of n)
+//   TF32          f32 (A: the caller's when k % 4 == 0), k innermost
+//   TF32X3        per 16-k block one 128-byte row: 16 tf32 hi, 16 tf32 lo
+//   TF32_BF16X2   per 16-k block one 128-byte row: 16 tf32 hi (64 B),
+//                 16 bf16(hi) (32 B), 16 bf16(x - hi) (32 B)
+// The interleaved rows let one 128-byte-swizzled TMA box carry every term a
+// stage needs; k beyond K inside the last block is zero.
+struct OperandView {
+    void* p = nullptr;
+    int64_t ld = 0;
 };
 
-// True when the mode reads A (resp. B) through pre-pass planes.
+struct GemmOperands {
+    int mode;
+    OperandView a;
+    OperandView b;
+};
+
+// True when the mode reads A (resp. B) through a pre-pass copy.
 bool gemm_a_needs_planes(int mode, int K);
 bool gemm_b_needs_planes(int mode);
-// Pitch (floats) of the pre-pass planes for inner dimension K.
-int64_t gemm_plane_pitch(int K);
+// Bytes of the prepared form of one operand with `outer` rows and reduction
+// K (256-byte aligned), and the view of such a buffer at `base`.
+uint64_t gemm_planes_bytes(int mode, int outer, int K);
+OperandView gemm_carve_planes(void* base, int mode, int outer, int K);
+// The same view `rows` rows further down.
+OperandView gemm_offset_rows(const OperandView& v, int64_t rows);
+// A caller operand read directly.
+OperandView gemm_raw_operand(const float* x, int64_t ld);
 
-// Pre-pass of A (M x K, pitch lda) into planes of pitch ldp; `lo` only for TF32X3.
-int gemm_prep_a(int mode, int M, int K, const float* A, int64_t lda, float* hi, float* lo,
-                int64_t ldp, cudaStream_t s);
-// Pre-pass of B (K x N, pitch ldb) into K-major B^T planes (N x K, pitch ldp).
-int gemm_prep_b(int mode, int K, int N, const float* B, int64_t ldb, float* hi, float* lo,
-                int64_t ldp, cudaStream_t s);
+// Pre-pass of A (M x K, pitch lda) into `out` (carved for mode, M, K).
+int gemm_prep_a(int mode, int M, int K, const float* A, int64_t lda, const OperandView& out,
+                cudaStream_t s);
+// Pre-pass of B (K x N, pitch ldb) into B^T form (carved for mode, N, K).
+int gemm_prep_b(int mode, int K, int N, const float* B, int64_t ldb, const OperandView& out,
+                cudaStream_t s);
 // C[M x N, pitch ldc] = epilogue(alpha * A @ B) on prepared operands.
 int gemm_run(const GemmOperands& op, int M, int N, int K, float alpha, float* C, int64_t ldc,
              const float* bias, int relu, cudaStream_t s);

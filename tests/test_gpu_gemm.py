@@ -273,3 +273,23 @@ def test_sharded_config_tiles_vs_fp64():
         assert O.rel_fro(c[r0:r0 + 128, c0:c0 + 128].cpu().numpy(), ref) <= 1e-5
     del ta, tb, c
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
+@pytest.mark.parametrize("m,n,k", [(2300, 2100, 1000), (4100, 4300, 72), (2176, 2432, 8200)])
+def test_cta_pair_path_shapes(mode, m, n, k):
+    """Shapes with enough 256 x 256 tiles to take the CTA-pair kernel, ragged in
+    every dimension (rows and columns past the last full tile, k not a multiple
+    of the stage depth)."""
+    ta = torch.from_numpy(O.uniform(m * k, 51).reshape(m, k)).cuda()
+    tb = torch.from_numpy(O.uniform(k * n, 52).reshape(k, n)).cuda()
+    tbias = torch.from_numpy(O.uniform(n, 53, -0.1, 0.1)).cuda()
+    c = K.sgemm(ta, tb, mode=mode, alpha=0.75, bias=tbias, relu=True)
+    torch.cuda.synchronize()
+    assert K.kernel_status() == 0
+    a, b = ta.cpu().numpy(), tb.cpu().numpy()
+    bias = tbias.cpu().numpy()
+    for r0, c0 in [(0, 0), (m - 128, n - 128), (m // 2 + 5, n // 3)]:
+        ref = np.maximum(0.75 * O.dgemm_tile(a, b, r0, c0, 128, 128) + bias[c0:c0 + 128], 0.0)
+        got = c[r0:r0 + 128, c0:c0 + 128].cpu().numpy()
+        assert O.rel_fro(got, ref) <= TOL[mode] * 1.5

@@ -47,6 +47,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -341,6 +342,252 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
+// ---- CTA-pair kernel (tcgen05 cta_group::2) -----------------------------------------
+// Two CTAs of a cluster compute one 256 x 256 tile: CTA r loads rows
+// [128r, 128r + 128) of the tile's A rows and of its B^T rows, and the leader
+// (r = 0) issues M = 256, N = 256 MMAs whose A and B halves come from both
+// CTAs' shared memory; each CTA's TMEM holds its 128 rows of D.  Per SM a stage
+// is 32 KB instead of 48 KB for the same MMA work, so six stages fit and the
+// L2 -> SM operand traffic per flop drops by a third.  Loads signal the
+// leader's full barrier (no multicast); the leader's commits arrive on both
+// CTAs' barriers; every epilogue warp of both CTAs frees a TMEM buffer on the
+// leader's barrier.
+constexpr int PBM = 256, PBN = 256;
+
+template <int S>
+struct PairCfg {
+    static constexpr int BK = S == 1 ? 32 : 16;
+    static constexpr int STAGES = 6;
+    static constexpr int A_BYTES = 128 * 128;  // this CTA's 128 rows x 128 B
+    static constexpr int B_BYTES = 128 * 128;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 32 KB
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*bars*/;
+    static constexpr int KB_PER_CHUNK = S >= 2 ? 512 / BK : (1 << 30);
+};
+
+constexpr uint32_t kIdescShapePair =
+    (static_cast<uint32_t>(PBN >> 3) << 17) | (static_cast<uint32_t>(PBM >> 4) << 24);
+constexpr uint32_t kIdescTf32Pair = (1u << 4) | (2u << 7) | (2u << 10) | kIdescShapePair;
+constexpr uint32_t kIdescBf16Pair = (1u << 4) | (1u << 7) | (1u << 10) | kIdescShapePair;
+
+template <int S>
+__device__ __forceinline__ void issue_stage_pair(uint32_t d_tmem, uint32_t stage_base,
+                                                 bool first) {
+    const uint32_t a = stage_base, b = stage_base + PairCfg<S>::A_BYTES;
+    auto d = [](uint32_t addr) { return umma_desc(addr, 16, 1024, 2); };
+    uint32_t acc = first ? 0u : 1u;
+    if (S == 3) {
+        mma_f16_ss_pair(d_tmem, d(a + 96), d(b + 64), kIdescBf16Pair, acc);
+        acc = 1u;
+        mma_f16_ss_pair(d_tmem, d(a + 64), d(b + 96), kIdescBf16Pair, 1u);
+    }
+#pragma unroll
+    for (int kk = 0; kk < (S == 1 ? 4 : 2); ++kk) {
+        const uint32_t ko = kk * 32;
+        if (S == 2) {
+            mma_tf32_ss_pair(d_tmem, d(a + 64 + ko), d(b + ko), kIdescTf32Pair, acc);
+            acc = 1u;
+            mma_tf32_ss_pair(d_tmem, d(a + ko), d(b + 64 + ko), kIdescTf32Pair, 1u);
+        }
+        mma_tf32_ss_pair(d_tmem, d(a + ko), d(b + ko), kIdescTf32Pair, acc);
+        acc = 1u;
+    }
+}
+
+template <int S>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
+    sgemm_tc_pair_kernel(const __grid_constant__ TcMaps maps, int M, int N, int K, float alpha,
+                         float* __restrict__ C, int64_t ldc, const float* __restrict__ bias,
+                         int relu, int vec_c) {
+    using Cfg = PairCfg<S>;
+    constexpr int BK = Cfg::BK, STAGES = Cfg::STAGES;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* acc_full = empty + STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* drain = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int mt = (M + PBM - 1) / PBM, nt = (N + PBN - 1) / PBN;
+    const int num_tiles = mt * nt;
+    const int nkb = (K + BK - 1) / BK;
+    const int nchunks = (nkb + Cfg::KB_PER_CHUNK - 1) / Cfg::KB_PER_CHUNK;
+    auto tile_origin = [&](int t, int& m0, int& n0) {
+        int mi, ni;
+        tile_coords(t, mt, nt, mi, ni);
+        m0 = mi * PBM;
+        n0 = ni * PBN;
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 2 * kEpiWarps);  // one arrive per epilogue warp, both CTAs
+        }
+        mbar_init(drain, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tensormap(&maps.a);
+        prefetch_tensormap(&maps.b);
+    }
+    if (warp == 1) tmem_alloc_pair(tmem_slot, kTmemCols);
+    tc_fence_before();
+    cluster_sync();  // both CTAs' barriers initialised, TMEM allocated in both
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer (both CTAs) ----------------
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int t = pair; t < num_tiles && ok; t += npairs) {
+                int m0, n0;
+                tile_origin(t, m0, n0);
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    if (!mbar_wait_bounded(&empty[s], ph ^ 1, &g_status, kErrTcProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    // The leader's full barrier counts both CTAs' bytes.
+                    if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
+                    const uint32_t bar = mapa_shared(&full[s], 0);
+                    uint8_t* st = smem + s * Cfg::STAGE_BYTES;
+                    tma_load_2d_pair(st, &maps.a, kb * 32, m0 + 128 * rank, bar);
+                    tma_load_2d_pair(st + Cfg::A_BYTES, &maps.b, kb * 32, n0 + 128 * rank, bar);
+                }
+            }
+            // No copy of this CTA may still be landing when it exits: wait until
+            // the leader's MMAs have consumed the last stages issued.
+            const int first = it > STAGES ? it - STAGES : 0;
+            for (int i = first; i < it; ++i)
+                mbar_wait_bounded(&empty[i % STAGES], (i / STAGES) & 1, &g_status, kErrTcDrain);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (leader only) ----------------
+        if (leader && lane == 0) {
+            bool ok = true;
+            int it = 0, cj = 0;
+            for (int t = pair; t < num_tiles && ok; t += npairs) {
+                for (int j = 0; j < nchunks && ok; ++j, ++cj) {
+                    const int buf = cj & 1;
+                    const uint32_t d_tmem = tmem_base + buf * PBN;
+                    if (cj >= 2 && !mbar_wait_bounded(&acc_empty[buf], ((cj >> 1) - 1) & 1,
+                                                      &g_status, kErrTcMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const int kb0 = j * Cfg::KB_PER_CHUNK;
+                    const int kb1 = min(nkb, kb0 + Cfg::KB_PER_CHUNK);
+                    for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                        const int s = it % STAGES;
+                        const uint32_t ph = (it / STAGES) & 1;
+                        if (!mbar_wait_bounded(&full[s], ph, &g_status, kErrTcMma)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        issue_stage_pair<S>(d_tmem, smem_u32(smem + s * Cfg::STAGE_BYTES),
+                                            kb == kb0);
+                        mma_commit_pair(&empty[s], 0x3);  // frees stage s in both CTAs
+                    }
+                    if (ok) mma_commit_pair(&acc_full[buf], 0x3);
+                }
+            }
+            if (!ok) {
+                mma_commit_pair(drain, 0x1);
+                mbar_wait_bounded(drain, 0, &g_status, kErrTcDrain);
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..9, both CTAs) ----------------
+        const int q = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + half * 128;
+        const uint32_t leader_empty0 = mapa_shared(&acc_empty[0], 0);
+        const uint32_t leader_empty1 = mapa_shared(&acc_empty[1], 0);
+        bool ok = true;
+        int cj = 0;
+        for (int t = pair; t < num_tiles && ok; t += npairs) {
+            int m0, n0;
+            tile_origin(t, m0, n0);
+            const int row = m0 + 128 * static_cast<int>(rank) + q * 32 + lane;
+            float acc[128];
+#pragma unroll
+            for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+            for (int j = 0; j < nchunks; ++j, ++cj) {
+                const int buf = cj & 1;
+                if (!mbar_wait_bounded(&acc_full[buf], (cj >> 1) & 1, &g_status,
+                                       kErrTcEpilogue)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(lane_base + buf * PBN + cc * 32, r);
+#pragma unroll
+                    for (int u = 0; u < 32; ++u) acc[cc * 32 + u] += __uint_as_float(r[u]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(buf ? leader_empty1 : leader_empty0);
+            }
+            if (ok && row < M) {
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    const int col0 = n0 + half * 128 + cc * 32;
+                    if (col0 < N) {
+                        float v[32];
+#pragma unroll
+                        for (int u = 0; u < 32; ++u) {
+                            float x = __fmul_rn(alpha, acc[cc * 32 + u]);
+                            if (bias) x = __fadd_rn(x, col0 + u < N ? __ldg(bias + col0 + u) : 0.0f);
+                            if (relu) x = relu1(x);
+                            v[u] = x;
+                        }
+                        float* dst = C + static_cast<int64_t>(row) * ldc + col0;
+                        if (vec_c && col0 + 32 <= N) {
+#pragma unroll
+                            for (int u = 0; u < 32; u += 4)
+                                *reinterpret_cast<float4*>(dst + u) =
+                                    make_float4(v[u], v[u + 1], v[u + 2], v[u + 3]);
+                        } else {
+#pragma unroll
+                            for (int u = 0; u < 32; ++u)
+                                if (col0 + u < N) dst[u] = v[u];
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, kTmemCols);
+    }
+}
+
 // ---- operand pre-pass ------------------------------------------------------------
 // Writes element (row r, k) of one operand view.  TF32 (S = 1): f32 copy;
 // TF32X3 (S = 2): block kb = k / 16 holds tf32(x) at [kb*32 + j] and
@@ -593,6 +840,38 @@ int launch_tc(const TcMaps& maps, int M, int N, int K, float alpha, float* C, in
 }
 
 template <int S>
+int launch_tc_pair(const TcMaps& maps, int M, int N, int K, float alpha, float* C, int64_t ldc,
+                   const float* bias, int relu, cudaStream_t s) {
+    using Cfg = PairCfg<S>;
+    static std::once_flag attr_once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(attr_once, [] {
+        attr_err = cudaFuncSetAttribute(sgemm_tc_pair_kernel<S>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        Cfg::SMEM_BYTES);
+    });
+    if (attr_err != cudaSuccess) return cuda_status(attr_err, "sgemm_tc_pair smem attribute");
+    const int tiles = ((M + PBM - 1) / PBM) * ((N + PBN - 1) / PBN);
+    const int vec_c = (ldc % 4 == 0) && aligned16(C);
+    // Persistent grid: one CTA pair per two SMs.
+    const int pairs = std::min(tiles, std::max(sm_count() / 2, 1));
+    sgemm_tc_pair_kernel<S><<<2 * pairs, kTcThreads, Cfg::SMEM_BYTES, s>>>(
+        maps, M, N, K, alpha, C, ldc, bias, relu, vec_c);
+    return cuda_status(cudaGetLastError(), "sgemm_tc_pair");
+}
+
+// CTA pairs pay off once there are enough 256 x 256 tiles to keep every SM
+// pair busy; smaller problems use one CTA per 128 x 256 tile.
+bool use_pairs(int M, int N) {
+    static const bool enabled = [] {
+        const char* e = std::getenv("ZENGPU_GEMM_PAIRS");
+        return !(e && e[0] == '0');
+    }();
+    const int tiles = ((M + PBM - 1) / PBM) * ((N + PBN - 1) / PBN);
+    return enabled && tiles >= sm_count() / 2;
+}
+
+template <int S>
 int run_tc(const GemmOperands& op, int M, int N, int K, float alpha, float* C, int64_t ldc,
            const float* bias, int relu, cudaStream_t s) {
     for (const OperandView* v : {&op.a, &op.b})
@@ -605,9 +884,12 @@ int run_tc(const GemmOperands& op, int M, int N, int K, float alpha, float* C, i
     const uint64_t cols = map_cols(op.mode, K);
     // TF32's A may be the caller's operand: its map covers exactly K columns
     const uint64_t acols = S == 1 ? static_cast<uint64_t>(K) : cols;
+    const bool pairs = use_pairs(M, N);
+    // Boxes: 128 rows of A per CTA; B^T 256 rows (one CTA) or 128 (each CTA of a pair).
     int rc = encode_map(&maps.a, op.a.p, acols, M, op.a.ld, BM);
-    if (!rc) rc = encode_map(&maps.b, op.b.p, cols, N, op.b.ld, BN);
+    if (!rc) rc = encode_map(&maps.b, op.b.p, cols, N, op.b.ld, pairs ? 128 : BN);
     if (rc) return rc;
+    if (pairs) return launch_tc_pair<S>(maps, M, N, K, alpha, C, ldc, bias, relu, s);
     return launch_tc<S>(maps, M, N, K, alpha, C, ldc, bias, relu, s);
 }
 

@@ -31,9 +31,8 @@ import datetime
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
+import threading
 import time
 from pathlib import Path
 
@@ -68,67 +67,88 @@ def env_ranks() -> tuple[int, int, int]:
 
 # ---- clocks -------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons over the timed region."""
+    """SM clock, power and clock-event reasons of one GPU, sampled every 10 ms
+    on a background thread while the `with` block (the timed region) runs.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    The GPU is found through NVML by the PCI bus id of the CUDA device, so the
+    samples belong to the GPU this process runs on whatever CUDA_VISIBLE_DEVICES
+    says.  `reader` (tests) replaces NVML: a callable returning
+    (sm_mhz, sm_max_mhz, power_w, set of active reason names)."""
+
     REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    PERIOD_S = 0.010
 
-    def __init__(self, gpu_index: int):
-        self.gpu_index = gpu_index
-        self.proc = None
-        self.path = None
+    def __init__(self, cuda_index: int = 0, reader=None):
+        self.cuda_index = cuda_index
+        self.reader = reader
+        self.samples: list[tuple[float, float, float, frozenset]] = []
+        self.error = None
+        self._stop = threading.Event()
+        self._thread = None
+
+    def _nvml_reader(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.cuda_index)
+        bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+        h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        bits = {"hw_slowdown": pynvml.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": pynvml.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": pynvml.nvmlClocksEventReasonSwPowerCap}
+        sm_max = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+
+        def read():
+            sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+            power = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+            mask = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+            return sm, sm_max, power, frozenset(n for n, b in bits.items() if mask & b)
+        return read
+
+    def _run(self):
+        while True:
+            try:
+                self.samples.append((time.monotonic(),) + tuple(self.reader()))
+            except Exception as e:  # noqa: BLE001 - reported in the summary
+                self.error = f"{type(e).__name__}: {e}"
+                return
+            if self._stop.wait(self.PERIOD_S):
+                return
 
     def __enter__(self):
-        fd, self.path = tempfile.mkstemp(suffix=".csv")
-        os.close(fd)
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-f", self.path], stdout=subprocess.DEVNULL,
-                stderr=subprocess.DEVNULL)
-            time.sleep(0.3)
-        except OSError:
-            self.proc = None
+        if self.reader is None:
+            try:
+                self.reader = self._nvml_reader()
+            except Exception as e:  # noqa: BLE001
+                self.error = f"NVML unavailable: {type(e).__name__}: {e}"
+                return self
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            time.sleep(0.25)
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
 
     def summary(self) -> dict:
-        rows = []
-        try:
-            for line in Path(self.path).read_text().splitlines():
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) >= 9 and parts[0].isdigit() and int(parts[0]) == self.gpu_index:
-                    rows.append(parts)
-        except OSError:
-            pass
-        finally:
-            if self.path:
-                try:
-                    os.unlink(self.path)
-                except OSError:
-                    pass
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        reasons = sorted({name for r in rows for name, v in zip(self.REASONS, r[5:9])
-                          if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
-                "samples": len(rows)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "source": "nvml", "error": self.error}
+        sm = [s[1] for s in self.samples]
+        reasons = sorted({r for s in self.samples for r in s[4]} & set(self.REASONS))
+        out = {"sm_mhz": statistics.median(sm), "sm_min_mhz": min(sm),
+               "sm_max_mhz": max(s[2] for s in self.samples),
+               "power_w_max": round(max(s[3] for s in self.samples), 1),
+               "reasons": reasons, "samples": len(self.samples),
+               "source": f"nvml every {int(self.PERIOD_S * 1000)} ms over the timed region"}
+        if self.error:
+            out["error"] = self.error
+        return out
 
 
-# ---- CPU backend baseline (the oracle restatement, bench.py's cpu leg only) ------------
 def _oracle():
     sys.path.insert(0, str(ROOT / "tests"))
     import _oracle
@@ -729,17 +749,21 @@ def mlp_workload(args, torch, zg, K, mode, peaks, peak_src, world):
         return h
 
     res = {}
+    clock_summary = None
     for name, fn in (("fused", fused), ("unfused", unfused)):
         for _ in range(args.warmup):
             fn()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(args.steps):
-            fn()
-        e1.record(stream)
-        torch.cuda.synchronize()
+        with ClockSampler(torch.cuda.current_device()) as clocks:
+            e0.record(stream)
+            for _ in range(args.steps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
         res[name] = e0.elapsed_time(e1) / args.steps
+        if name == "fused":
+            clock_summary = clocks.summary()
     flops = layers * 2.0 * bsz * hid * hid
     return {
         "metric": METRIC, "value": flops / (res["fused"] * 1e-3) / 1e12, "unit": "TFLOP/s",
@@ -749,7 +773,10 @@ def mlp_workload(args, torch, zg, K, mode, peaks, peak_src, world):
         "config": {"workload": f"op_graph_lower MLP 4 x relu(X@W+b), 4096x4096, {args.mode}",
                    "unfused_ms_per_step": res["unfused"],
                    "speedup_fused_vs_unfused": res["unfused"] / res["fused"]},
-        "gpu_launches": args.steps * layers * (3 if mode == 1 else 1),
+        # per layer: TF32X3 / TF32_BF16X2 pack A, pack B, kernel; TF32 transpose B,
+        # kernel; SIMT one kernel
+        "gpu_launches": args.steps * layers * {1: 3, 2: 2, 3: 3}.get(int(mode), 1),
+        "clocks": clock_summary,
     }
 
 

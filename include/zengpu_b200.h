@@ -376,6 +376,45 @@ int zg_fill_normal_f32(float *x, uint64_t n, uint64_t seed, void *stream);
  * in time, else a bitmask of the kernels whose wait expired.  Synchronises. */
 int zg_kernel_status(uint32_t *code);
 
+/* ---- B broadcast along a chain of GPUs (row-sharded GEMM, one process per
+ * GPU).  No counterpart in the reference: ZenGPU has no collective; its only
+ * multi-device operation is a HIP peer copy (zengpu-hip/src/lib.rs:609-710).
+ *
+ * Ranks 0 -> 1 -> ... -> W-1 each create a chain object (same mode, k, n,
+ * chunk_cols on every rank), exchange the 64-byte CUDA IPC handles by any
+ * means, and connect to their neighbours.  Each step e (1, 2, ..., the same
+ * on every rank) then runs:
+ *   rank 0      zg_bchain_source(e, B): packs B^T into the tensor-core operand
+ *               form chunk by chunk (chunk_cols columns of B each, a multiple
+ *               of 256), raising each chunk's flag;
+ *   every rank  zg_bchain_forward(e) on a copy stream: pushes each chunk, once
+ *               its flag is up, to the next rank with a copy-engine peer copy
+ *               and raises the flag there (no SMs used);
+ *               zg_bchain_gemm(e, gated): C = epilogue(alpha * A @ B) with A
+ *               packed by zg_sgemm_pack_a; gated = 1 lets the kernel start at
+ *               once and hold back the B loads of chunks not yet arrived (the
+ *               rank that ran zg_bchain_source on the same stream passes 0);
+ *               zg_bchain_release(e) on a stream ordered after both: tells the
+ *               previous rank this rank's buffer of step e may be reused.
+ * Two buffers alternate between steps.  A wait that can never end (a rank
+ * that died) is ended by zg_bchain_abort on the waiting ranks; the GEMM's own
+ * gate gives up after 2 s and reports ZG_ERR_KERNEL_WAIT through
+ * zg_kernel_status.  Tensor-core modes only. */
+#define ZG_IPC_HANDLE_BYTES 64
+typedef struct zg_bchain zg_bchain;
+int zg_bchain_create(int mode, int k, int n, int chunk_cols, zg_bchain **out, uint8_t *handle);
+int zg_bchain_connect(zg_bchain *chain, const uint8_t *prev_handle, const uint8_t *next_handle);
+int zg_bchain_source(zg_bchain *chain, uint32_t epoch, const float *b, int64_t ldb, void *stream);
+int zg_bchain_forward(zg_bchain *chain, uint32_t epoch, void *stream);
+int zg_bchain_gemm(zg_bchain *chain, uint32_t epoch, int gated, int m, float alpha,
+                   const void *a_packed, float *c, int64_t ldc, const float *bias, int relu,
+                   void *stream);
+int zg_bchain_release(zg_bchain *chain, uint32_t epoch, void *stream);
+/* The packed B^T buffer step `epoch` uses, and its size in bytes. */
+int zg_bchain_buffer(const zg_bchain *chain, uint32_t epoch, const void **ptr, uint64_t *bytes);
+int zg_bchain_abort(zg_bchain *chain, uint32_t epoch);
+int zg_bchain_destroy(zg_bchain *chain);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -104,3 +104,19 @@ def test_product_path_does_not_reference_the_oracle():
     pkg = Path(zg.__file__).resolve().parent
     for p in list(pkg.rglob("*.py")) + list(pkg.rglob("*.cu")) + list(pkg.rglob("*.cpp")):
         assert "oracle" not in p.read_text().lower(), p
+
+
+def test_bchain_argument_errors_need_no_gpu():
+    """The chain's argument checks answer before any CUDA call."""
+    lib = zg.load_library()
+    out = C.c_void_p()
+    handle = (C.c_uint8 * 64)()
+    # SIMT has no chunked B^T form; chunks must be multiples of 256 columns
+    assert lib.zg_bchain_create(0, 64, 512, 256, C.byref(out), handle) == zg.api.Dispatch.code
+    assert lib.zg_bchain_create(3, 64, 512, 200, C.byref(out), handle) == zg.api.Dispatch.code
+    assert lib.zg_bchain_create(3, 0, 512, 256, C.byref(out), handle) == zg.api.Dispatch.code
+    assert out.value is None
+    assert lib.zg_bchain_forward(None, 1, None) == zg.api.Dispatch.code
+    assert lib.zg_bchain_gemm(None, 1, 1, 8, 1.0, None, None, 512, None, 0, None) == \
+        zg.api.Dispatch.code
+    assert lib.zg_bchain_destroy(None) == 0

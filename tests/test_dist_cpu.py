@@ -150,3 +150,178 @@ def test_panel_count():
     assert panel_count(4096, 32768) == 4
     assert panel_count(1024, 8192) == 1      # too small to split
     assert panel_count(32768, 32768) == 8
+
+
+# ---- chained copy-engine broadcast: host-side protocol ------------------------------
+from zengpu_b200.dist import ChainedGemm, chain_neighbours, default_chunk_cols  # noqa: E402
+
+
+@pytest.mark.parametrize("world,src", [(1, 0), (2, 0), (8, 0), (8, 3), (3, 2)])
+def test_chain_neighbours_form_one_chain(world, src):
+    order = [src]
+    while True:
+        _, nxt = chain_neighbours(order[-1], world, src)
+        if nxt is None:
+            break
+        order.append(nxt)
+    assert sorted(order) == list(range(world))
+    for i, r in enumerate(order):
+        prev, nxt = chain_neighbours(r, world, src)
+        assert prev == (order[i - 1] if i > 0 else None)
+        assert nxt == (order[i + 1] if i + 1 < world else None)
+
+
+def test_default_chunk_cols():
+    assert default_chunk_cols(8192, 8192) == 256          # 16 MiB packed at k = 8192
+    assert default_chunk_cols(32768, 1024) == 2048
+    assert default_chunk_cols(300, 16) == 512             # never more than n rounded to 256
+    for n, k in [(8192, 8192), (32768, 8192), (1000, 77)]:
+        assert default_chunk_cols(n, k) % 256 == 0
+
+
+class _FakeStream:
+    cuda_stream = 0
+
+    def __init__(self, log=None, name="copy"):
+        self.log, self.name = log, name
+
+    def wait_stream(self, other):
+        if self.log is not None:
+            self.log.append(("wait_stream", other.name))
+
+
+class _FakeBuf:
+    def data_ptr(self):
+        return 0x2000
+
+
+class _FakePacked:
+    buf = _FakeBuf()
+
+
+class _FakeOps:
+    def __init__(self, log):
+        self.log = log
+
+    def pack_a(self, a, mode, out=None):
+        self.log.append(("pack_a", tuple(a.shape)))
+        return _FakePacked()
+
+
+class _FakeChainLib:
+    """Records the C calls of one rank; the IPC handle is the rank number."""
+
+    def __init__(self, rank, log):
+        self.rank, self.log = rank, log
+
+    def zg_bchain_create(self, mode, k, n, chunk, out, handle):
+        out._obj.value = 0x1000 + self.rank
+        for i in range(64):
+            handle[i] = self.rank
+        self.log.append(("create", mode, k, n, chunk))
+        return 0
+
+    def zg_bchain_connect(self, chain, prev, nxt):
+        self.log.append(("connect", None if prev is None else prev[0],
+                         None if nxt is None else nxt[0]))
+        return 0
+
+    def zg_bchain_source(self, chain, epoch, b, ldb, stream):
+        self.log.append(("source", epoch))
+        return 0
+
+    def zg_bchain_forward(self, chain, epoch, stream):
+        self.log.append(("forward", epoch))
+        return 0
+
+    def zg_bchain_gemm(self, chain, epoch, gated, m, alpha, pa, c, ldc, bias, relu, stream):
+        self.log.append(("gemm", epoch, gated, m))
+        return 0
+
+    def zg_bchain_release(self, chain, epoch, stream):
+        self.log.append(("release", epoch))
+        return 0
+
+    def zg_bchain_destroy(self, chain):
+        self.log.append(("destroy",))
+        return 0
+
+
+def _worker_chain(rank, world, port, src, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        log = []
+        torch.cuda.current_stream = lambda: _FakeStream(log, "compute")
+        cg = ChainedGemm(k=64, n=512, mode=3, src=src, chunk_cols=256,
+                         lib=_FakeChainLib(rank, log), ops=_FakeOps(log))
+        cg.copy_stream = _FakeStream(log, "copy")
+        a = torch.zeros((10, 64))
+        b = torch.zeros((64, 512)) if rank == src else None
+        out = torch.zeros((10, 512))
+        for _ in range(3):
+            cg.step(a, b, out)
+        cg.close()
+        q.put((rank, log))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,src", [(3, 0), (3, 1)])
+def test_chained_gemm_call_protocol(world, src):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_chain, args=(r, world, port, src, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    logs = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, log in logs.items():
+        prev, nxt = chain_neighbours(rank, world, src)
+        assert log[0] == ("create", 3, 64, 512, 256)
+        assert log[1] == ("connect", prev, nxt)   # neighbours' handles, by rank
+        steps = log[2:-1]
+        assert log[-1] == ("destroy",)
+        per_step = 6 if rank == src else 5
+        assert len(steps) == 3 * per_step
+        for i in range(3):
+            e = i + 1
+            s = steps[i * per_step:(i + 1) * per_step]
+            expect = ([("source", e)] if rank == src else []) + [
+                ("forward", e), ("pack_a", (10, 64)), ("gemm", e, 0 if rank == src else 1, 10),
+                ("wait_stream", "copy"), ("release", e)]
+            assert s == expect
+
+
+def _worker_chain_mismatch(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        log = []
+        try:
+            ChainedGemm(k=64, n=512 + 256 * rank, mode=3, chunk_cols=256,
+                        lib=_FakeChainLib(rank, log), ops=_FakeOps(log))
+            q.put((rank, "no error"))
+        except ValueError as e:
+            q.put((rank, "disagree" in str(e) and ("destroy",) in log))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_chained_gemm_rejects_mismatched_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_chain_mismatch, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: True, 1: True}

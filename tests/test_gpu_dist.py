@@ -1,0 +1,109 @@
+"""Row-sharded GEMM on several GPUs, one process per GPU (needs >= 2 GPUs).
+
+ChainedGemm carries B from the source rank along the chain by the copy
+engines while every rank's GEMM runs; each rank's rows of C must equal, bit
+for bit, the single-GPU GEMM of the same rows (same packed operands, same
+kernel).  B changes every step, so both chain buffers and the reuse
+hand-shake between ranks are exercised."""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, mode, m_total, n, k, chunk, src, steps, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    from zengpu_b200 import kernels as K
+    from zengpu_b200.dist import ChainedGemm, row_range
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    result = {"rank": rank, "ok": False}
+    try:
+        r0, r1 = row_range(m_total, world, rank)
+        a_full = K.fill_uniform(torch.empty((m_total, k), device="cuda"), 7)
+        a = a_full[r0:r1].contiguous()
+        cg = ChainedGemm(k, n, mode=mode, src=src, chunk_cols=chunk)
+        out = torch.empty((r1 - r0, n), device="cuda")
+        bias = K.fill_uniform(torch.empty(n, device="cuda"), 9, -0.1, 0.1)
+        mismatches = []
+        for step in range(steps):
+            # every rank can make the same B; only the source's copy is used
+            b_full = K.fill_uniform(torch.empty((k, n), device="cuda"), 100 + step)
+            relu = step % 2 == 1
+            cg.step(a, b_full if rank == src else None, out, alpha=0.5,
+                    bias=bias if relu else None, relu=relu)
+            ref = K.sgemm(a, b_full, mode=mode, alpha=0.5, bias=bias if relu else None,
+                          relu=relu)
+            torch.cuda.synchronize()
+            if not torch.equal(out.view(torch.int32), ref.view(torch.int32)):
+                diff = (out - ref).abs().max().item()
+                mismatches.append((step, diff))
+        status = K.kernel_status()
+        cg.close()
+        result.update(ok=not mismatches and status == 0, mismatches=mismatches, status=status)
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        result["error"] = f"{type(e).__name__}: {e}"
+    finally:
+        q.put(result)
+        dist.destroy_process_group()
+
+
+def _run(world, **kw):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    args = (kw["mode"], kw["m_total"], kw["n"], kw["k"], kw["chunk"], kw.get("src", 0),
+            kw.get("steps", 4))
+    # daemonic: a rank left waiting on a peer that failed dies with the test
+    procs = [ctx.Process(target=_worker, args=(r, world, port) + args + (q,), daemon=True)
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+    for r in sorted(results, key=lambda r: r["rank"]):
+        assert r["ok"], r
+    for p in procs:
+        assert p.exitcode == 0
+
+
+@pytest.mark.parametrize("mode", [3, 1, 2], ids=["TF32_BF16X2", "TF32X3", "TF32"])
+def test_chained_gemm_two_ranks(mode):
+    # 2 x 1024 rows: 128 x 256 tiles (single-CTA kernel); chunks of 256 columns
+    _run(2, mode=mode, m_total=2048, n=4096, k=1024, chunk=256)
+
+
+def test_chained_gemm_pair_kernel_ragged():
+    # 2 x 2050 rows, n not a multiple of the chunk, k not a multiple of 16:
+    # enough 256 x 256 tiles for the CTA-pair kernel
+    _run(2, mode=3, m_total=4100, n=4000, k=2072, chunk=512)
+
+
+def test_chained_gemm_source_not_rank0():
+    _run(2, mode=3, m_total=1024, n=2048, k=512, chunk=256, src=1)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four GPUs")
+def test_chained_gemm_four_ranks():
+    _run(4, mode=3, m_total=4096, n=4096, k=1024, chunk=256, src=2)

@@ -293,3 +293,27 @@ def test_cta_pair_path_shapes(mode, m, n, k):
         ref = np.maximum(0.75 * O.dgemm_tile(a, b, r0, c0, 128, 128) + bias[c0:c0 + 128], 0.0)
         got = c[r0:r0 + 128, c0:c0 + 128].cpu().numpy()
         assert O.rel_fro(got, ref) <= TOL[mode] * 1.5
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two visible GPUs")
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
+def test_second_device_in_one_process(mode):
+    """The kernels' launch attributes are per device: the same process runs the
+    GEMM on device 0, then on device 1, then on device 0 again, and all three
+    agree bit for bit (same kernel, same inputs)."""
+    m, n, k = 2048, 2304, 520
+    a = O.uniform(m * k, 61).reshape(m, k)
+    b = O.uniform(k * n, 62).reshape(k, n)
+    outs = []
+    for dev in (0, 1, 0):
+        with torch.cuda.device(dev):
+            ta = torch.from_numpy(a).to(f"cuda:{dev}")
+            tb = torch.from_numpy(b).to(f"cuda:{dev}")
+            c = K.sgemm(ta, tb, mode=mode)
+            torch.cuda.synchronize(dev)
+            assert K.kernel_status() == 0
+            outs.append(c.cpu().numpy())
+    assert np.array_equal(bits(outs[0]), bits(outs[1]))
+    assert np.array_equal(bits(outs[0]), bits(outs[2]))
+    ref = O.dgemm_tile(a, b, 0, 0, 128, 128)
+    assert O.rel_fro(outs[1][:128, :128], ref) <= TOL[mode] * 1.5

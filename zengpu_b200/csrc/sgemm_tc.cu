@@ -46,6 +46,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
@@ -158,7 +159,7 @@ template <int S>
 __global__ void __launch_bounds__(kTcThreads, 1)
     sgemm_tc_kernel(const __grid_constant__ TcMaps maps, int M, int N, int K, float alpha,
                     float* __restrict__ C, int64_t ldc, const float* __restrict__ bias, int relu,
-                    int vec_c) {
+                    int vec_c, const GemmGate gate) {
     using Cfg = TcCfg<S>;
     constexpr int BK = Cfg::BK, STAGES = Cfg::STAGES;
 
@@ -215,6 +216,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
                 int m0, n0;
                 tile_origin(t, m0, n0);
+                if (gate.flags && !flag_wait_bounded(gate.flags + n0 / gate.rows, gate.epoch,
+                                                     &g_status, kErrTcGate)) {
+                    ok = false;
+                    break;
+                }
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
@@ -398,7 +404,7 @@ template <int S>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     sgemm_tc_pair_kernel(const __grid_constant__ TcMaps maps, int M, int N, int K, float alpha,
                          float* __restrict__ C, int64_t ldc, const float* __restrict__ bias,
-                         int relu, int vec_c) {
+                         int relu, int vec_c, const GemmGate gate) {
     using Cfg = PairCfg<S>;
     constexpr int BK = Cfg::BK, STAGES = Cfg::STAGES;
 
@@ -457,6 +463,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
             for (int t = pair; t < num_tiles && ok; t += npairs) {
                 int m0, n0;
                 tile_origin(t, m0, n0);
+                // both CTAs' B halves lie in the chunk of n0 (chunks are 256-row multiples)
+                if (gate.flags && !flag_wait_bounded(gate.flags + n0 / gate.rows, gate.epoch,
+                                                     &g_status, kErrTcGate)) {
+                    ok = false;
+                    break;
+                }
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
@@ -818,45 +830,50 @@ int launch_prep_transpose(int mode, const float* src, int K, int N, int64_t lds,
     return cuda_status(cudaGetLastError(), "sgemm transpose pre-pass");
 }
 
+// The opt-in shared-memory size is a per-device attribute of a kernel: it is
+// set the first time the kernel is launched on each device of the process.
+template <typename Kern>
+cudaError_t ensure_smem_attr(Kern* kern, int bytes, std::atomic<uint64_t>& done) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = dev < 64 ? (uint64_t{1} << dev) : 0;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_release);
+    return e;
+}
+
 template <int S>
 int launch_tc(const TcMaps& maps, int M, int N, int K, float alpha, float* C, int64_t ldc,
-              const float* bias, int relu, cudaStream_t s) {
+              const float* bias, int relu, cudaStream_t s, const GemmGate& gate) {
     using Cfg = TcCfg<S>;
-    static std::once_flag attr_once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(attr_once, [] {
-        attr_err = cudaFuncSetAttribute(sgemm_tc_kernel<S>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        Cfg::SMEM_BYTES);
-    });
+    static std::atomic<uint64_t> attr_done{0};
+    const cudaError_t attr_err = ensure_smem_attr(sgemm_tc_kernel<S>, Cfg::SMEM_BYTES, attr_done);
     if (attr_err != cudaSuccess) return cuda_status(attr_err, "sgemm_tc smem attribute");
     const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
     const int vec_c = (ldc % 4 == 0) && aligned16(C);
     // Persistent grid: one CTA per SM (the smem footprint allows no more).
     const int grid = std::min(mt * nt, sm_count());
     sgemm_tc_kernel<S><<<grid, kTcThreads, Cfg::SMEM_BYTES, s>>>(maps, M, N, K, alpha, C, ldc,
-                                                                bias, relu, vec_c);
+                                                                bias, relu, vec_c, gate);
     return cuda_status(cudaGetLastError(), "sgemm_tc");
 }
 
 template <int S>
 int launch_tc_pair(const TcMaps& maps, int M, int N, int K, float alpha, float* C, int64_t ldc,
-                   const float* bias, int relu, cudaStream_t s) {
+                   const float* bias, int relu, cudaStream_t s, const GemmGate& gate) {
     using Cfg = PairCfg<S>;
-    static std::once_flag attr_once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(attr_once, [] {
-        attr_err = cudaFuncSetAttribute(sgemm_tc_pair_kernel<S>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        Cfg::SMEM_BYTES);
-    });
+    static std::atomic<uint64_t> attr_done{0};
+    const cudaError_t attr_err =
+        ensure_smem_attr(sgemm_tc_pair_kernel<S>, Cfg::SMEM_BYTES, attr_done);
     if (attr_err != cudaSuccess) return cuda_status(attr_err, "sgemm_tc_pair smem attribute");
     const int tiles = ((M + PBM - 1) / PBM) * ((N + PBN - 1) / PBN);
     const int vec_c = (ldc % 4 == 0) && aligned16(C);
     // Persistent grid: one CTA pair per two SMs.
     const int pairs = std::min(tiles, std::max(sm_count() / 2, 1));
     sgemm_tc_pair_kernel<S><<<2 * pairs, kTcThreads, Cfg::SMEM_BYTES, s>>>(
-        maps, M, N, K, alpha, C, ldc, bias, relu, vec_c);
+        maps, M, N, K, alpha, C, ldc, bias, relu, vec_c, gate);
     return cuda_status(cudaGetLastError(), "sgemm_tc_pair");
 }
 
@@ -873,7 +890,11 @@ bool use_pairs(int M, int N) {
 
 template <int S>
 int run_tc(const GemmOperands& op, int M, int N, int K, float alpha, float* C, int64_t ldc,
-           const float* bias, int relu, cudaStream_t s) {
+           const float* bias, int relu, cudaStream_t s, const GemmGate* gate) {
+    const GemmGate g = gate ? *gate : GemmGate{};
+    if (g.flags && (g.rows <= 0 || g.rows % 256 != 0))
+        return set_error(ZG_ERR_DISPATCH, "sgemm: gate chunk of %d rows is not a multiple of 256",
+                         g.rows);
     for (const OperandView* v : {&op.a, &op.b})
         if (!v->p || !aligned16(v->p) || v->ld % 4 != 0)
             return set_error(ZG_ERR_DISPATCH,
@@ -889,8 +910,8 @@ int run_tc(const GemmOperands& op, int M, int N, int K, float alpha, float* C, i
     int rc = encode_map(&maps.a, op.a.p, acols, M, op.a.ld, BM);
     if (!rc) rc = encode_map(&maps.b, op.b.p, cols, N, op.b.ld, pairs ? 128 : BN);
     if (rc) return rc;
-    if (pairs) return launch_tc_pair<S>(maps, M, N, K, alpha, C, ldc, bias, relu, s);
-    return launch_tc<S>(maps, M, N, K, alpha, C, ldc, bias, relu, s);
+    if (pairs) return launch_tc_pair<S>(maps, M, N, K, alpha, C, ldc, bias, relu, s, g);
+    return launch_tc<S>(maps, M, N, K, alpha, C, ldc, bias, relu, s, g);
 }
 
 }  // namespace
@@ -941,15 +962,18 @@ int gemm_prep_b(int mode, int K, int N, const float* B, int64_t ldb, const Opera
 }
 
 int gemm_run(const GemmOperands& op, int M, int N, int K, float alpha, float* C, int64_t ldc,
-             const float* bias, int relu, cudaStream_t s) {
+             const float* bias, int relu, cudaStream_t s, const GemmGate* gate) {
+    if (gate && gate->flags && op.mode == ZG_GEMM_SIMT_FP32)
+        return set_error(ZG_ERR_DISPATCH, "sgemm: the arrival gate needs a tensor-core mode");
     switch (op.mode) {
         case ZG_GEMM_SIMT_FP32:
             return launch_sgemm_simt(M, N, K, alpha, static_cast<const float*>(op.a.p), op.a.ld,
                                      static_cast<const float*>(op.b.p), op.b.ld, C, ldc, bias,
                                      relu, s);
-        case ZG_GEMM_TF32: return run_tc<1>(op, M, N, K, alpha, C, ldc, bias, relu, s);
-        case ZG_GEMM_TF32X3: return run_tc<2>(op, M, N, K, alpha, C, ldc, bias, relu, s);
-        case ZG_GEMM_TF32_BF16X2: return run_tc<3>(op, M, N, K, alpha, C, ldc, bias, relu, s);
+        case ZG_GEMM_TF32: return run_tc<1>(op, M, N, K, alpha, C, ldc, bias, relu, s, gate);
+        case ZG_GEMM_TF32X3: return run_tc<2>(op, M, N, K, alpha, C, ldc, bias, relu, s, gate);
+        case ZG_GEMM_TF32_BF16X2:
+            return run_tc<3>(op, M, N, K, alpha, C, ldc, bias, relu, s, gate);
         default: return set_error(ZG_ERR_DISPATCH, "sgemm: unknown mode %d", op.mode);
     }
 }

@@ -17,6 +17,7 @@ enum : uint32_t {
     kErrTcMma = 1u << 1,
     kErrTcEpilogue = 1u << 2,
     kErrTcDrain = 1u << 3,
+    kErrTcGate = 1u << 4,  // a B chunk never arrived (multi-GPU arrival gate)
 };
 
 // Every on-device wait gives up after this long and reports instead of
@@ -79,6 +80,33 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
             return false;
         }
     }
+}
+
+// Waits until *flag has reached `epoch` (wrap-aware), for data another GPU's
+// copy engine writes into this GPU's memory and then flags with a release
+// write.  The acquire load orders this thread's later loads after the data;
+// the proxy fence extends that to the TMA (async proxy) loads it issues next.
+// Gives up like mbar_wait_bounded.
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ bool flag_wait_bounded(const uint32_t* flag, uint32_t epoch,
+                                                  uint32_t* status, uint32_t err_bit) {
+    if (static_cast<int32_t>(ld_acquire_sys_u32(flag) - epoch) < 0) {
+        const uint64_t t0 = globaltimer_ns();
+        while (static_cast<int32_t>(ld_acquire_sys_u32(flag) - epoch) < 0) {
+            __nanosleep(128);
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(status, err_bit);
+                return false;
+            }
+        }
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    return true;
 }
 
 // ---- TMA -------------------------------------------------------------------

@@ -49,8 +49,21 @@ int gemm_prep_a(int mode, int M, int K, const float* A, int64_t lda, const Opera
 // Pre-pass of B (K x N, pitch ldb) into B^T form (carved for mode, N, K).
 int gemm_prep_b(int mode, int K, int N, const float* B, int64_t ldb, const OperandView& out,
                 cudaStream_t s);
-// C[M x N, pitch ldc] = epilogue(alpha * A @ B) on prepared operands.
+// Arrival gate of a GEMM whose B^T rows are still landing in its buffer
+// (copied from another GPU while the GEMM runs): rows [c * rows, (c + 1) *
+// rows) of B^T may be read once flags[c] has reached `epoch` (wrap-aware:
+// (int32_t)(flags[c] - epoch) >= 0).  `rows` is a multiple of 256, so every
+// output tile's B rows sit in one chunk.  The tensor-core kernels check the
+// flag once per tile before loading its B rows.
+struct GemmGate {
+    const uint32_t* flags = nullptr;
+    uint32_t epoch = 0;
+    int rows = 0;
+};
+
+// C[M x N, pitch ldc] = epilogue(alpha * A @ B) on prepared operands; `gate`
+// (tensor-core modes only) holds back B loads until their chunk has arrived.
 int gemm_run(const GemmOperands& op, int M, int N, int K, float alpha, float* C, int64_t ldc,
-             const float* bias, int relu, cudaStream_t s);
+             const float* bias, int relu, cudaStream_t s, const GemmGate* gate = nullptr);
 
 }  // namespace zg

@@ -157,3 +157,127 @@ class ShardedGemm:
         parts = [torch.empty_like(padded) for _ in range(self.world)]
         dist.all_gather(parts, padded, group=self.group)
         return torch.cat([p[: r1 - r0] for p, (r0, r1) in zip(parts, counts)], dim=0)
+
+
+def chain_neighbours(rank: int, world: int, src: int = 0) -> tuple[int | None, int | None]:
+    """(previous, next) rank of `rank` in the broadcast chain src -> src+1 ->
+    ... (mod world); None at the chain's two ends."""
+    if world <= 0 or not 0 <= rank < world or not 0 <= src < world:
+        raise ValueError(f"bad rank {rank} / src {src} of {world}")
+    pos = (rank - src) % world
+    prev = (rank - 1) % world if pos > 0 else None
+    nxt = (rank + 1) % world if pos < world - 1 else None
+    return prev, nxt
+
+
+def default_chunk_cols(n: int, k: int, target_bytes: int = 16 << 20, bytes_per_elem: int = 8) -> int:
+    """Columns of B per chunk of the chained broadcast: a multiple of 256 whose
+    packed size is about `target_bytes` (large enough for a copy engine to run
+    near NVLink speed, small enough that the last rank starts early)."""
+    cols = max(256, (target_bytes // max(1, k * bytes_per_elem)) // 256 * 256)
+    return min(cols, ((n + 255) // 256) * 256)
+
+
+class ChainedGemm:
+    """C[row0:row1] = epilogue(alpha * A[row0:row1] @ B) on every rank, with B
+    carried from rank `src` along the chain src -> src+1 -> ... by the copy
+    engines while every rank's GEMM already runs (zg_bchain_* in the C ABI).
+
+    B is packed once, on `src`, into the tensor-core operand form; chunks of
+    it hop rank to rank over NVLink, and each rank's GEMM waits per output
+    tile only for the chunk that tile reads.  No SM is spent on the transfer,
+    and no collective library is on the data path.  The process group is used
+    once, to exchange the CUDA IPC handles of the chain buffers."""
+
+    def __init__(self, k: int, n: int, mode: int = 3, group=None, src: int = 0,
+                 chunk_cols: int | None = None, lib=None, ops=None):
+        import ctypes as C
+
+        from . import _lib as L
+        from .api import check
+
+        self._C, self._check = C, check
+        self.lib = lib if lib is not None else L.load()
+        if ops is None:
+            from . import kernels as ops
+        self.ops = ops
+        self.group, self.src, self.mode, self.k, self.n = group, src, int(mode), k, n
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        bpe = 4 if self.mode == 2 else 8
+        self.chunk_cols = chunk_cols or default_chunk_cols(n, k, bytes_per_elem=bpe)
+        self.prev, self.next = chain_neighbours(self.rank, self.world, src)
+
+        handle = (C.c_uint8 * 64)()
+        ptr = C.c_void_p()
+        check(self.lib.zg_bchain_create(self.mode, k, n, self.chunk_cols, C.byref(ptr), handle))
+        self.chain = ptr
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, (bytes(handle), (self.mode, k, n, self.chunk_cols)),
+                               group=group)
+        if any(cfg != everyone[self.rank][1] for _, cfg in everyone):
+            self.lib.zg_bchain_destroy(self.chain)
+            raise ValueError(f"ChainedGemm: ranks disagree on (mode, k, n, chunk): "
+                             f"{[cfg for _, cfg in everyone]}")
+
+        def buf(r):
+            return None if r is None else (C.c_uint8 * 64).from_buffer_copy(everyone[r][0])
+
+        check(self.lib.zg_bchain_connect(self.chain, buf(self.prev), buf(self.next)))
+        dist.barrier(group=group)
+        self.copy_stream = torch.cuda.Stream() if torch.cuda.is_available() else None
+        self.epoch = 0
+        self._packed_a = None
+
+    def step(self, a_rows: torch.Tensor, b: torch.Tensor | None, out: torch.Tensor,
+             alpha: float = 1.0, bias: torch.Tensor | None = None,
+             relu: bool = False) -> torch.Tensor:
+        """One sharded GEMM.  `b` [k, n] is read on `src` only (others may pass
+        None); `out` [rows, n] (row pitch out.stride(0)) receives this rank's
+        rows of C."""
+        C = self._C
+        if a_rows.dim() != 2 or a_rows.shape[1] != self.k:
+            raise ValueError(f"ChainedGemm: A rows must be [m, {self.k}]")
+        m = a_rows.shape[0]
+        if tuple(out.shape) != (m, self.n) or out.stride(1) != 1:
+            raise ValueError(f"ChainedGemm: out must be [{m}, {self.n}] with unit column stride")
+        self.epoch += 1
+        e = self.epoch & 0xFFFFFFFF
+        compute = torch.cuda.current_stream()
+        cs = C.c_void_p(compute.cuda_stream)
+        copy = C.c_void_p(self.copy_stream.cuda_stream)
+        is_src = self.rank == self.src
+        if is_src:
+            if b is None or tuple(b.shape) != (self.k, self.n) or b.stride(1) != 1:
+                raise ValueError(f"ChainedGemm: the source rank needs B [{self.k}, {self.n}]")
+            # packs chunk by chunk; each chunk's flag lets the copy stream push it on
+            self._check(self.lib.zg_bchain_source(self.chain, e, b.data_ptr(), b.stride(0), cs))
+        self._check(self.lib.zg_bchain_forward(self.chain, e, copy))
+        self._packed_a = self.ops.pack_a(
+            a_rows, self.mode, out=self._packed_a.buf if self._packed_a is not None else None)
+        self._check(self.lib.zg_bchain_gemm(
+            self.chain, e, 0 if is_src else 1, m, float(alpha), self._packed_a.buf.data_ptr(),
+            out.data_ptr(), out.stride(0), bias.data_ptr() if bias is not None else None,
+            1 if relu else 0, cs))
+        # this rank's buffer of step e is free once its GEMM and its forwarding are done
+        compute.wait_stream(self.copy_stream)
+        self._check(self.lib.zg_bchain_release(self.chain, e, cs))
+        return out
+
+    def packed_b(self, epoch: int | None = None) -> tuple[int, int]:
+        """(device pointer, bytes) of the packed B^T buffer of a step."""
+        C = self._C
+        p, nb = C.c_void_p(), C.c_uint64()
+        e = (self.epoch if epoch is None else epoch) & 0xFFFFFFFF
+        self._check(self.lib.zg_bchain_buffer(self.chain, e, C.byref(p), C.byref(nb)))
+        return p.value, nb.value
+
+    def close(self) -> None:
+        """Frees the chain after every rank is done with every step."""
+        if self.chain is None:
+            return
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self._check(self.lib.zg_bchain_destroy(self.chain))
+        self.chain = None

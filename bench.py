@@ -232,6 +232,12 @@ def main() -> int:
     ap.add_argument("--panels", type=int, default=1,
                     help="N > 1: column panels of the B broadcast (1 = whole B, overlapped "
                          "with packing A)")
+    ap.add_argument("--bcast", choices=["chain", "nccl"], default="chain",
+                    help="N > 1: how B reaches every rank - packed once on rank 0 and pushed "
+                         "rank to rank by the copy engines under the running GEMMs (chain), or "
+                         "an NCCL broadcast of raw B before each rank packs it (nccl)")
+    ap.add_argument("--chunk-cols", type=int, default=0,
+                    help="chain: columns of B per chunk (multiple of 256; 0 = ~16 MiB packed)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the e2e / elementwise / cpu-baseline legs")
     args = ap.parse_args()
@@ -306,6 +312,15 @@ def ours(args, rank: int, local_rank: int, world: int) -> int:
     return 0
 
 
+def _gather_floats(torch, dist, world, value: float) -> list[float]:
+    if world == 1:
+        return [value]
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t)
+    return [round(float(p.item()), 4) for p in parts]
+
+
 def _max_over_ranks(torch, dist, world, value: float) -> float:
     if world == 1:
         return value
@@ -355,7 +370,17 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
         if ev1 is not None:
             ev1.record(stream)
 
-    if world > 1:
+    chain = None
+    if world > 1 and args.bcast == "chain":
+        # B is packed once on rank 0 and pushed rank to rank by the copy engines
+        # while every rank's GEMM runs, gated per chunk (dist.ChainedGemm).
+        from zengpu_b200.dist import ChainedGemm
+        chain = ChainedGemm(k, n, mode=int(mode), src=0, chunk_cols=args.chunk_cols or None)
+        panels = 1
+
+        def step(ev0=None, ev1=None):
+            chain.step(a, b if rank == 0 else None, c)
+    elif world > 1:
         # B arrives from rank 0 in column panels; panel j+1 crosses NVLink while
         # panel j is multiplied (dist.ShardedGemm.sgemm_rows_pipelined).
         from zengpu_b200.dist import ShardedGemm
@@ -389,6 +414,18 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
         if world > 1:
             dist.barrier()
     ms_local = t0.elapsed_time(t1) / args.steps
+    if K.kernel_status() != 0:
+        raise RuntimeError("bounded on-device wait expired during timing")
+    if world > 1 and rank != 0:
+        # B reached this rank only through the broadcast; the accuracy check and
+        # the kernel-only timing use the same B, regenerated from its seed
+        K.fill_uniform(b, 1002)
+    # the last timed step's C of every rank, checked before anything rewrites it
+    accuracy = sampled_accuracy(torch, dist, a, b, c, mode, world)
+    chain_desc = None
+    if chain is not None:
+        chain_desc = (chain.chunks, chain.chunk_cols)
+        chain.close()
     if world > 1:
         # the dominant kernel alone: one full-shard launch per rank, same stream
         for _ in range(2):
@@ -400,11 +437,10 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
     else:
         kern_ms_local = statistics.mean(e0.elapsed_time(e1) for e0, e1 in kev)
     ms = _max_over_ranks(torch, dist, world, ms_local)
+    ms_by_rank = _gather_floats(torch, dist, world, ms_local)
     kern_ms = _max_over_ranks(torch, dist, world, kern_ms_local)
     if K.kernel_status() != 0:
-        raise RuntimeError("bounded on-device wait expired during timing")
-
-    accuracy = sampled_accuracy(torch, a, b, c, mode, rank, world)
+        raise RuntimeError("bounded on-device wait expired in the kernel-only timing")
     other = {}
     if not args.no_extras and args.workload == "gemm" and mode == zg.GemmMode.TF32_BF16X2:
         other["tf32x3"] = kernel_only(torch, lib, zg.GemmMode.TF32X3, a, b, c, m_local, n, k, sp,
@@ -421,8 +457,11 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
             zg.GemmMode.TF32_BF16X2: tf32_peak / 2.0}[mode]
     # N = 1: TF32X3 split(A) + transpose-split(B) + tcgen05 kernel; TF32:
     # transpose(B) (+ a pitched copy of A when k % 4 != 0) + kernel; SIMT: one.
-    # N > 1: pack(A) + per column panel pack(B panel) + kernel.
-    if world > 1:
+    # N > 1, chain (rank 0): pack(B) in one launch that flags each chunk, then
+    # pack(A) + kernel; nccl: pack(A) + per column panel pack(B panel) + kernel.
+    if chain_desc is not None:
+        launches_per_step = 3
+    elif world > 1:
         launches_per_step = 1 + 2 * panels
     else:
         launches_per_step = {zg.GemmMode.TF32X3: 3, zg.GemmMode.TF32: 2 + (k % 4 != 0),
@@ -444,9 +483,12 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
         "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: A, B uniform[-1,1) from the splitmix64 generator (seeds 2, 1002)",
         "config": {"workload": workload, "m": m_total, "n": n, "k": k, "mode": args.mode,
-                   "parallelism": f"dp{world} (A/C row blocks, B broadcast over NCCL"
-                                  + (f" in {panels} column panels overlapped with the GEMM)"
-                                     if world > 1 else ")"),
+                   "parallelism": (f"dp{world} (A/C row blocks; B packed on rank 0 and pushed "
+                                   f"rank to rank over NVLink by the copy engines in "
+                                   f"{chain_desc[0]} chunks of {chain_desc[1]} columns, each "
+                                   f"rank's GEMM gated per chunk)" if chain_desc is not None else
+                                   f"dp{world} (A/C row blocks, B broadcast over NCCL"
+                                   + (f" in {panels} column panels)" if world > 1 else ")")),
                    "l2": "inputs larger than L2: A, B 256 MiB each, plus 1 GiB of hi/lo planes"},
         "roofline": {"bound": "tensor" if mode != zg.GemmMode.SIMT_FP32 else "fp32",
                      "kernel": f"sgemm_tc_kernel<{ {1: 2, 2: 1, 3: 3}.get(int(mode), 0)}>"
@@ -468,6 +510,8 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
     }
+    if world > 1:
+        line["ms_per_step_by_rank"] = ms_by_rank
     line["accuracy"] = accuracy
     if other:
         line["other_modes"] = other
@@ -480,23 +524,22 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
     return line
 
 
-def sampled_accuracy(torch, a, b, c, mode, rank, world) -> dict:
-    """Relative Frobenius error of a 256 x 256 block of this rank's C against a
-    float64 product of the same operands (numpy on the host)."""
+def sampled_accuracy(torch, dist, a, b, c, mode, world) -> dict:
+    """Relative Frobenius error of a 256 x 256 block of each rank's C against a
+    float64 product of the same operands (numpy on the host); max over ranks."""
     import numpy as np
     import zengpu_b200 as zg
     r0 = min(1000, max(a.shape[0] - 256, 0))
     c0 = min(3000, max(b.shape[1] - 256, 0))
     rows = a[r0:r0 + 256].double().cpu().numpy()
     cols = b[:, c0:c0 + 256].double().cpu().numpy()
-    if world > 1 and rank != 0:
-        return {"skipped": "B on this rank is not the broadcast value after timing"}
     ref = rows @ cols
     got = c[r0:r0 + 256, c0:c0 + 256].double().cpu().numpy()
-    err = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
+    err = _max_over_ranks(torch, dist, world,
+                          float(np.linalg.norm(got - ref) / np.linalg.norm(ref)))
     bar = 5e-3 if mode == zg.GemmMode.TF32 else 1e-5
     return {"rel_fro_vs_fp64": err, "bar": bar, "block": [r0, c0, 256, 256],
-            "within_bar": err <= bar}
+            "ranks": world, "within_bar": err <= bar}
 
 
 def kernel_only(torch, lib, mode, a, b, c, m, n, k, sp, stream, dist, world, reps: int = 5):
@@ -516,7 +559,7 @@ def kernel_only(torch, lib, mode, a, b, c, m, n, k, sp, stream, dist, world, rep
         e1.record(stream)
     torch.cuda.synchronize()
     ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs[2:])
-    acc = sampled_accuracy(torch, a, b, c, mode, 0, 1)
+    acc = sampled_accuracy(torch, None, a, b, c, mode, 1)
     del ws
     torch.cuda.empty_cache()
     return {"kernel_ms": ms, "kernel_tflops": 2.0 * m * n * k / (ms * 1e-3) / 1e12,
@@ -566,16 +609,28 @@ def gemm_e2e(args, torch, dist, zg, K, mode, m_local, n, k, m_total, world, loca
     else:
         a = torch.empty((m_local, k), device="cuda")
         b = torch.empty((k, n), device="cuda")
-        from zengpu_b200.dist import ShardedGemm
-        sg = ShardedGemm(mode=int(mode))
+        c = torch.empty((m_local, n), device="cuda")
         rank = dist.get_rank()
         stream = torch.cuda.current_stream()
+        chain = None
+        if args.bcast == "chain":
+            from zengpu_b200.dist import ChainedGemm
+            chain = ChainedGemm(k, n, mode=int(mode), src=0, chunk_cols=args.chunk_cols or None)
+
+            def gemm_rows():
+                chain.step(a, b if rank == 0 else None, c)
+        else:
+            from zengpu_b200.dist import ShardedGemm
+            sg = ShardedGemm(mode=int(mode))
+
+            def gemm_rows():
+                sg.sgemm_rows_pipelined(a, b, src=0, panels=max(1, args.panels), out=c)
 
         def step():
             a.copy_(ha, non_blocking=True)
             if rank == 0:
                 b.copy_(hb, non_blocking=True)
-            c = sg.sgemm_rows_pipelined(a, b, src=0, panels=max(1, args.panels))
+            gemm_rows()
             hc.copy_(c, non_blocking=True)
 
         for _ in range(2):
@@ -589,6 +644,8 @@ def gemm_e2e(args, torch, dist, zg, K, mode, m_local, n, k, m_total, world, loca
         e1.record(stream)
         torch.cuda.synchronize()
         dt = _max_over_ranks(torch, dist, world, e0.elapsed_time(e1) / steps / 1e3)
+        if chain is not None:
+            chain.close()
         h2d = ha.numel() * 4 + (hb.numel() * 4 if rank == 0 else 0)
         clock = "CUDA events on the compute stream, max over ranks"
     total_flops = 2.0 * m_total * n * k

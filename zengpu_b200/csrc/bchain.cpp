@@ -95,7 +95,7 @@ struct zg_bchain {
     int mode = 0, k = 0, n = 0, chunk_cols = 0, chunks = 0;
     int64_t ld = 0;               // packed B^T row pitch, 4-byte units
     uint64_t buf_bytes = 0;       // one packed B buffer
-    uint64_t off_flags = 0, off_done = 0, total = 0;
+    uint64_t off_flags = 0, off_done = 0, off_count = 0, total = 0;
     uint8_t* base = nullptr;      // this rank's allocation
     uint8_t* prev = nullptr;      // upstream rank's allocation (IPC), or null
     uint8_t* next = nullptr;      // downstream rank's allocation (IPC), or null
@@ -105,6 +105,7 @@ struct zg_bchain {
         return reinterpret_cast<uint32_t*>(b + off_flags) + (epoch & 1u) * chunks;
     }
     uint32_t* done(uint8_t* b) const { return reinterpret_cast<uint32_t*>(b + off_done); }
+    uint32_t* counters() const { return reinterpret_cast<uint32_t*>(base + off_count); }
     int chunk_rows(int c) const {
         const int r0 = c * chunk_cols;
         return (n - r0 < chunk_cols) ? n - r0 : chunk_cols;
@@ -150,7 +151,8 @@ extern "C" int zg_bchain_create(int mode, int k, int n, int chunk_cols, zg_bchai
     c->buf_bytes = round256(zg::gemm_planes_bytes(mode, n, k));
     c->off_flags = 2 * c->buf_bytes;
     c->off_done = c->off_flags + round256(2ull * c->chunks * sizeof(uint32_t));
-    c->total = c->off_done + 256;
+    c->off_count = c->off_done + 256;
+    c->total = c->off_count + round256(static_cast<uint64_t>(c->chunks) * sizeof(uint32_t));
     cudaError_t e = cudaMalloc(&c->base, c->total);
     if (e != cudaSuccess) {
         delete c;
@@ -204,15 +206,9 @@ extern "C" int zg_bchain_source(zg_bchain* c, uint32_t epoch, const float* b, in
     if (!b || ldb < c->n) return set_error(ZG_ERR_DISPATCH, "bchain_source: bad B");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const zg::OperandView view = zg::gemm_carve_planes(c->buf(c->base, epoch), c->mode, c->n, c->k);
-    uint32_t* flags = c->flags(c->base, epoch);
-    for (int ch = 0; ch < c->chunks; ++ch) {
-        const int col0 = ch * c->chunk_cols;
-        int rc = zg::gemm_prep_b(c->mode, c->k, c->chunk_rows(ch), b + col0, ldb,
-                                 zg::gemm_offset_rows(view, col0), s);
-        if (!rc) rc = write_flag(flags + ch, epoch, s);
-        if (rc) return rc;
-    }
-    return ZG_OK;
+    // one launch; its last CTA of each chunk raises that chunk's flag
+    return zg::gemm_prep_b_signal(c->mode, c->k, c->n, b, ldb, view, c->chunk_cols,
+                                  c->counters(), c->flags(c->base, epoch), epoch, s);
 }
 
 extern "C" int zg_bchain_forward(zg_bchain* c, uint32_t epoch, void* stream) {

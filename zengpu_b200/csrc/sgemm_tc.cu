@@ -703,6 +703,48 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// The transpose pre-pass of B for a chunked hand-off: CTAs run k-block
+// fastest, so column strips (and chunks of chunk_cols columns) finish in
+// order, and the last CTA of chunk c publishes flags[c] = epoch with a
+// system-scope release (the copy engine and other GPUs read the chunk after
+// seeing it).  counters[] (one per chunk) start at zero.
+template <int S>
+__global__ void __launch_bounds__(256)
+    prep_transpose_signal_kernel(const float* __restrict__ src, int K, int N, int64_t lds,
+                                 float* dst, int64_t ldd, int kpad, int chunk_cols,
+                                 uint32_t* counters, uint32_t* flags, uint32_t epoch) {
+    __shared__ float tile[32][33];
+    const int k0 = blockIdx.x * 32, n0 = blockIdx.y * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+#pragma unroll
+    for (int j = ty; j < 32; j += 8) {
+        const int k = k0 + j, n = n0 + tx;
+        tile[j][tx] = (k < K && n < N) ? __ldcs(src + static_cast<int64_t>(k) * lds + n) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = ty; j < 32; j += 8) {
+        const int n = n0 + j, k = k0 + tx;
+        if (n < N && k < kpad) put_value<S>(dst, ldd, n, k, tile[tx][j]);
+    }
+    __threadfence();  // this thread's part of the chunk, before the CTA is counted
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int c = n0 / chunk_cols;
+        const int c_end = min(N, (c + 1) * chunk_cols);
+        const uint32_t expected =
+            static_cast<uint32_t>((c_end - c * chunk_cols + 31) / 32) * gridDim.x;
+        uint32_t prev;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                     : "=r"(prev)
+                     : "l"(counters + c)
+                     : "memory");
+        if (prev + 1 == expected)
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flags + c), "r"(epoch)
+                         : "memory");
+    }
+}
+
 // Plain pitched copy (SIMT packing of B).
 __global__ void __launch_bounds__(256)
     copy_rows_kernel(const float* __restrict__ src, int rows, int cols, int64_t lds,
@@ -828,6 +870,26 @@ int launch_prep_transpose(int mode, const float* src, int K, int N, int64_t lds,
         default: return set_error(ZG_ERR_DISPATCH, "sgemm pre-pass: no planes for mode %d", mode);
     }
     return cuda_status(cudaGetLastError(), "sgemm transpose pre-pass");
+}
+
+int launch_prep_transpose_signal(int mode, const float* src, int K, int N, int64_t lds,
+                                 const OperandView& v, int chunk_cols, uint32_t* counters,
+                                 uint32_t* flags, uint32_t epoch, cudaStream_t s) {
+    if (K == 0 || N == 0) return ZG_OK;
+    const int kpad = static_cast<int>(view_kpad(mode, K));
+    const int chunks = (N + chunk_cols - 1) / chunk_cols;
+    dim3 grid((kpad + 31) / 32, (N + 31) / 32);
+    if (grid.y > 65535u) return set_error(ZG_ERR_DISPATCH, "sgemm: n too large for the pre-pass");
+    cudaError_t e = cudaMemsetAsync(counters, 0, static_cast<size_t>(chunks) * sizeof(uint32_t), s);
+    if (e != cudaSuccess) return cuda_status(e, "sgemm chunked pre-pass: counters");
+    float* dst = static_cast<float*>(v.p);
+    switch (scheme_of(mode)) {
+        case 1: prep_transpose_signal_kernel<1><<<grid, 256, 0, s>>>(src, K, N, lds, dst, v.ld, kpad, chunk_cols, counters, flags, epoch); break;
+        case 2: prep_transpose_signal_kernel<2><<<grid, 256, 0, s>>>(src, K, N, lds, dst, v.ld, kpad, chunk_cols, counters, flags, epoch); break;
+        case 3: prep_transpose_signal_kernel<3><<<grid, 256, 0, s>>>(src, K, N, lds, dst, v.ld, kpad, chunk_cols, counters, flags, epoch); break;
+        default: return set_error(ZG_ERR_DISPATCH, "sgemm pre-pass: no planes for mode %d", mode);
+    }
+    return cuda_status(cudaGetLastError(), "sgemm chunked transpose pre-pass");
 }
 
 // The opt-in shared-memory size is a per-device attribute of a kernel: it is
@@ -959,6 +1021,17 @@ int gemm_prep_b(int mode, int K, int N, const float* B, int64_t ldb, const Opera
                 cudaStream_t s) {
     if (!gemm_b_needs_planes(mode)) return ZG_OK;
     return launch_prep_transpose(mode, B, K, N, ldb, out, s);
+}
+
+int gemm_prep_b_signal(int mode, int K, int N, const float* B, int64_t ldb,
+                       const OperandView& out, int chunk_cols, uint32_t* counters,
+                       uint32_t* flags, uint32_t epoch, cudaStream_t s) {
+    if (!gemm_b_needs_planes(mode))
+        return set_error(ZG_ERR_DISPATCH, "sgemm: mode %d has no B^T pre-pass", mode);
+    if (chunk_cols <= 0 || chunk_cols % 32 != 0)
+        return set_error(ZG_ERR_DISPATCH, "sgemm: chunk of %d columns", chunk_cols);
+    return launch_prep_transpose_signal(mode, B, K, N, ldb, out, chunk_cols, counters, flags,
+                                        epoch, s);
 }
 
 int gemm_run(const GemmOperands& op, int M, int N, int K, float alpha, float* C, int64_t ldc,

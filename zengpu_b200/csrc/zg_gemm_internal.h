@@ -49,6 +49,14 @@ int gemm_prep_a(int mode, int M, int K, const float* A, int64_t lda, const Opera
 // Pre-pass of B (K x N, pitch ldb) into B^T form (carved for mode, N, K).
 int gemm_prep_b(int mode, int K, int N, const float* B, int64_t ldb, const OperandView& out,
                 cudaStream_t s);
+// gemm_prep_b, in one launch that raises flags[c] = epoch (system-scope
+// release) as soon as chunk c (columns [c * chunk_cols, ...) of B, rows of
+// B^T) is fully written; chunks finish in order.  counters: one u32 per
+// chunk, device memory, reset by the call.
+int gemm_prep_b_signal(int mode, int K, int N, const float* B, int64_t ldb,
+                       const OperandView& out, int chunk_cols, uint32_t* counters,
+                       uint32_t* flags, uint32_t epoch, cudaStream_t s);
+
 // Arrival gate of a GEMM whose B^T rows are still landing in its buffer
 // (copied from another GPU while the GEMM runs): rows [c * rows, (c + 1) *
 // rows) of B^T may be read once flags[c] has reached `epoch` (wrap-aware:

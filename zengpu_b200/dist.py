@@ -206,6 +206,7 @@ class ChainedGemm:
         self.world = dist.get_world_size(group)
         bpe = 4 if self.mode == 2 else 8
         self.chunk_cols = chunk_cols or default_chunk_cols(n, k, bytes_per_elem=bpe)
+        self.chunks = (n + self.chunk_cols - 1) // self.chunk_cols
         self.prev, self.next = chain_neighbours(self.rank, self.world, src)
 
         handle = (C.c_uint8 * 64)()

@@ -2,18 +2,20 @@
 """Benchmark of the ZenGPU compute hot path on B200.
 
 Default workload (one JSON line on rank 0):
-  f32 GEMM, 3xTF32 tensor-core mode (fp32-class accuracy), M = N = K = 8192
-  per GPU.  With N GPUs each rank owns an 8192-row block of A and C (weak
-  scaling, M = 8192 * N); B (8192 x 8192) is broadcast from rank 0 over NCCL
-  every step - the path's only exchange - then every rank runs the split
-  pre-pass and the tcgen05 GEMM on its block.
+  f32 GEMM, BF16X3 tensor-core mode (each f32 operand split into bf16 hi +
+  lo, three bf16 products; rel-Frobenius error ~4e-6 against float64, inside
+  the 1e-5 bar of the fp32-class modes), M = N = K = 8192 per GPU.  With N
+  GPUs each rank owns an 8192-row block of A and C (weak scaling, M = 8192 *
+  N); every step B (8192 x 8192) is packed on rank 0 and carried rank to rank
+  over NVLink by the copy engines while every rank's GEMM runs (--bcast nccl:
+  an NCCL broadcast first) - the path's only exchange.
 
   value       whole-job useful TFLOP/s (2*M*N*K per step over all ranks),
               device-timed with CUDA events, max over ranks
   e2e         the same GEMM through the drop-in API (CudaDevice + BufferPool +
               GemmKernel at N=1; torch tensors + dist at N>1) with host
               buffers: pinned H2D of A and B, GEMM, D2H of C, every step
-  roofline    the tcgen05 kernel alone against the 3xTF32 ceiling
+  roofline    the tcgen05 kernel alone against its mode's tensor ceiling
   cpu_baseline the CPU backend's algorithm (the oracle's C restatement of
               zengpu-cpu's loop) on a bounded row sample, all host cores
   elementwise add (z = x + y) and in-place ReLU on 2^28 f32 (1 GiB each)
@@ -46,10 +48,13 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # dominant kernel, from one ncu capture of the same workload on a B200:
 #   --set full -k regex:sgemm_tc_kernel on `bench.py --steps 1 --warmup 3 --no-extras`
 #   --section MemoryWorkloadAnalysis -k regex:stream_vec_kernel on the elementwise workload
+# Keyed by the kernel and the per-rank GEMM size (M = N = K) or element count.
 NCU_TRAFFIC = {
-    ("gemm", "tf32bf16", 8192): 4.841e9,
-    ("gemm", "tf32x3", 8192): 4.869e9,
-    ("elementwise", "add", 1 << 28): 3.188e9,
+    ("sgemm_tc_pair_kernel<3>", 8192): 5.642e9,
+    ("sgemm_tc_pair_kernel<2>", 8192): 5.999e9,
+    ("sgemm_tc_kernel<3>", 8192): 4.841e9,
+    ("sgemm_tc_kernel<2>", 8192): 4.869e9,
+    ("stream_vec_kernel<AddOp>", 1 << 28): 3.188e9,
 }
 
 
@@ -225,9 +230,10 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["gemm", "mlp", "sharded", "elementwise"],
                     default="gemm")
-    ap.add_argument("--mode", choices=["tf32x3", "tf32", "simt", "tf32bf16"], default="tf32bf16",
-                    help="GEMM arithmetic; tf32bf16 and tf32x3 are the fp32-accurate "
-                         "(rel-Frobenius <= 1e-5) tensor-core modes")
+    ap.add_argument("--mode", choices=["tf32x3", "tf32", "simt", "tf32bf16", "bf16x3"],
+                    default="bf16x3",
+                    help="GEMM arithmetic; bf16x3, tf32bf16 and tf32x3 are the fp32-accurate "
+                         "(rel-Frobenius <= 1e-5) tensor-core modes, tf32 the fast one (5e-3)")
     ap.add_argument("--size", type=int, default=8192)
     ap.add_argument("--panels", type=int, default=1,
                     help="N > 1: column panels of the B broadcast (1 = whole B, overlapped "
@@ -293,7 +299,8 @@ def ours(args, rank: int, local_rank: int, world: int) -> int:
                                 device_id=dev)
     peaks, peak_src = load_peaks()
     mode = {"tf32x3": zg.GemmMode.TF32X3, "tf32": zg.GemmMode.TF32,
-            "simt": zg.GemmMode.SIMT_FP32, "tf32bf16": zg.GemmMode.TF32_BF16X2}[args.mode]
+            "simt": zg.GemmMode.SIMT_FP32, "tf32bf16": zg.GemmMode.TF32_BF16X2,
+            "bf16x3": zg.GemmMode.BF16X3}[args.mode]
     try:
         if args.workload == "mlp":
             line = mlp_workload(args, torch, zg, K, mode, peaks, peak_src, world)
@@ -442,19 +449,26 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
     if K.kernel_status() != 0:
         raise RuntimeError("bounded on-device wait expired in the kernel-only timing")
     other = {}
-    if not args.no_extras and args.workload == "gemm" and mode == zg.GemmMode.TF32_BF16X2:
-        other["tf32x3"] = kernel_only(torch, lib, zg.GemmMode.TF32X3, a, b, c, m_local, n, k, sp,
-                                      stream, dist, world)
+    fp32_class = {"tf32x3": zg.GemmMode.TF32X3, "tf32bf16": zg.GemmMode.TF32_BF16X2,
+                  "bf16x3": zg.GemmMode.BF16X3}
+    if not args.no_extras and args.workload == "gemm" and mode in fp32_class.values():
+        # the other fp32-accurate modes' kernels on the same operands, for comparison
+        for name, other_mode in fp32_class.items():
+            if other_mode != mode:
+                other[name] = kernel_only(torch, lib, other_mode, a, b, c, m_local, n, k, sp,
+                                          stream, dist, world)
     total_flops = 2.0 * m_total * n * k
     value = total_flops / (ms * 1e-3) / 1e12
     rank_flops = 2.0 * m_local * n * k
     achieved = rank_flops / (kern_ms * 1e-3) / 1e12
     tf32_peak = peaks["bf16_tflops"] / 2.0
     fp32_simt_peak = 148 * 128 * 2 * 1.965e9 / 1e12  # SMs x FP32 lanes x FMA x max clock
-    # TF32_BF16X2: one tf32 product + two bf16 products at twice the tf32 rate
+    # TF32_BF16X2: one tf32 product + two bf16 products at twice the tf32 rate;
+    # BF16X3: three bf16 products
     peak = {zg.GemmMode.TF32X3: tf32_peak / 3.0, zg.GemmMode.TF32: tf32_peak,
             zg.GemmMode.SIMT_FP32: fp32_simt_peak,
-            zg.GemmMode.TF32_BF16X2: tf32_peak / 2.0}[mode]
+            zg.GemmMode.TF32_BF16X2: tf32_peak / 2.0,
+            zg.GemmMode.BF16X3: peaks["bf16_tflops"] / 3.0}[mode]
     # N = 1: TF32X3 split(A) + transpose-split(B) + tcgen05 kernel; TF32:
     # transpose(B) (+ a pitched copy of A when k % 4 != 0) + kernel; SIMT: one.
     # N > 1, chain (rank 0): pack(B) in one launch that flags each chunk, then
@@ -465,7 +479,8 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
         launches_per_step = 1 + 2 * panels
     else:
         launches_per_step = {zg.GemmMode.TF32X3: 3, zg.GemmMode.TF32: 2 + (k % 4 != 0),
-                             zg.GemmMode.SIMT_FP32: 1, zg.GemmMode.TF32_BF16X2: 3}[mode]
+                             zg.GemmMode.SIMT_FP32: 1, zg.GemmMode.TF32_BF16X2: 3,
+                             zg.GemmMode.BF16X3: 3}[mode]
 
     extras = {}
     e2e = None
@@ -487,19 +502,22 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
                                    f"rank to rank over NVLink by the copy engines in "
                                    f"{chain_desc[0]} chunks of {chain_desc[1]} columns, each "
                                    f"rank's GEMM gated per chunk)" if chain_desc is not None else
-                                   f"dp{world} (A/C row blocks, B broadcast over NCCL"
-                                   + (f" in {panels} column panels)" if world > 1 else ")")),
+                                   f"dp{world} (A/C row blocks, B broadcast over NCCL in "
+                                   f"{panels} column panels)" if world > 1 else
+                                   "dp1 (one GPU, no exchange)"),
                    "l2": "inputs larger than L2: A, B 256 MiB each, plus 1 GiB of hi/lo planes"},
         "roofline": {"bound": "tensor" if mode != zg.GemmMode.SIMT_FP32 else "fp32",
-                     "kernel": f"sgemm_tc_kernel<{ {1: 2, 2: 1, 3: 3}.get(int(mode), 0)}>"
-                     if mode != zg.GemmMode.SIMT_FP32 else "sgemm_simt_kernel",
+                     "kernel": tc_kernel_name(torch, int(mode), m_local, n),
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak,
-                     "traffic": NCU_TRAFFIC.get(("gemm", args.mode, s))
+                     "traffic": NCU_TRAFFIC.get((tc_kernel_name(torch, int(mode), m_local, n), s))
                      if args.workload == "gemm" else None,
                      "algorithmic_bytes": algorithmic_bytes(mode, m_local, n, k),
                      "kernel_ms": kern_ms,
-                     "peak_basis": (f"{peak_src} bf16 {peaks['bf16_tflops']} TFLOP/s / 2 (tf32 "
+                     "peak_basis": (f"{peak_src} bf16 {peaks['bf16_tflops']} TFLOP/s / 3 "
+                                    "(three bf16 MMAs per useful product)"
+                                    if mode == zg.GemmMode.BF16X3 else
+                                    f"{peak_src} bf16 {peaks['bf16_tflops']} TFLOP/s / 2 (tf32 "
                                     "rate)" + {zg.GemmMode.TF32X3: " / 3 (tf32 MMAs per useful "
                                                "product)",
                                                zg.GemmMode.TF32_BF16X2: " / 2 (one tf32 + two "
@@ -522,6 +540,19 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
                                 "kind": "port", "sample": cpu["sample"]}
     line.update(extras)
     return line
+
+
+def tc_kernel_name(torch, mode: int, m: int, n: int) -> str:
+    """The GEMM kernel the library launches for an m x n output (its rule: the
+    CTA-pair kernel once there is a 256 x 256 tile for every SM pair, unless
+    ZENGPU_GEMM_PAIRS=0)."""
+    if mode == 0:
+        return "sgemm_simt_kernel"
+    scheme = {1: 2, 2: 1, 3: 3, 4: 4}[mode]
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    pairs = (-(-m // 256)) * (-(-n // 256)) >= sms // 2 and os.environ.get(
+        "ZENGPU_GEMM_PAIRS", "1")[:1] != "0"
+    return f"sgemm_tc_pair_kernel<{scheme}>" if pairs else f"sgemm_tc_kernel<{scheme}>"
 
 
 def sampled_accuracy(torch, dist, a, b, c, mode, world) -> dict:
@@ -570,7 +601,7 @@ def algorithmic_bytes(mode: int, m: int, n: int, k: int) -> int:
     """Bytes the GEMM kernel must move once: its operand planes in, C out."""
     if mode == 0:  # SIMT reads A and B directly
         return 4 * (m * k + k * n + m * n)
-    per_elem = {1: 8, 2: 4, 3: 8}[int(mode)]  # tf32 hi+lo / f32 / tf32 + 2 bf16
+    per_elem = {1: 8, 2: 4, 3: 8, 4: 4}[int(mode)]  # tf32 hi+lo / f32 / tf32 + 2 bf16 / 2 bf16
     return per_elem * (m * k + n * k) + 4 * m * n
 
 
@@ -735,7 +766,7 @@ def elementwise_workload(args, torch, dist, K, peaks, peak_src, rank, local_rank
                    "parallelism": f"{world} independent contiguous chunks, no collective"},
         "roofline": {"bound": "hbm", "kernel": "stream_vec_kernel<AddOp>", "achieved": add_gbs,
                      "peak": peak, "unit": "GB/s", "frac": add_gbs / peak,
-                     "traffic": NCU_TRAFFIC.get(("elementwise", "add", n)),
+                     "traffic": NCU_TRAFFIC.get(("stream_vec_kernel<AddOp>", n)),
                      "algorithmic_bytes": 12 * n,
                      "kernel_ms": add_ms, "peak_basis": f"{peak_src} hbm_gbs",
                      "relu_inplace": {"achieved": relu_gbs, "frac": relu_gbs / peak,

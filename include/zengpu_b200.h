@@ -97,11 +97,14 @@ typedef struct zg_handle {
  * lo*hi, three TF32 products (rel-Frobenius <= 1e-5).  TF32: one tcgen05 TF32
  * pass (<= 5e-3).  TF32_BF16X2: the same split with the two small correction
  * products in bf16 (twice the TF32 rate), 2/3 of TF32X3's tensor time
- * (rel-Frobenius <= 1e-5). */
+ * (rel-Frobenius <= 1e-5).  BF16X3: x = bf16 hi + bf16 lo for both operands,
+ * hi*hi + hi*lo + lo*hi as three bf16 products, 1/2 of TF32X3's tensor time
+ * and half its operand bytes (rel-Frobenius <= 1e-5). */
 #define ZG_GEMM_SIMT_FP32 0
 #define ZG_GEMM_TF32X3 1
 #define ZG_GEMM_TF32 2
 #define ZG_GEMM_TF32_BF16X2 3
+#define ZG_GEMM_BF16X3 4
 
 /* ======================================================================
  * 1. Device runtime

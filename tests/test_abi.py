@@ -58,6 +58,10 @@ def test_workspace_bytes():
     assert lib.zg_sgemm_workspace_bytes(3, 8192, 8192, 8192) == 4 * 8192 * 8192 * 4
     assert lib.zg_sgemm_workspace_bytes(1, 17, 9, 33) == 256 * ((17 * 96 * 4 + 255) // 256) + \
         256 * ((9 * 96 * 4 + 255) // 256)
+    # BF16X3: each 32-k block one 128-byte row (32 bf16 hi, 32 bf16 lo), k padded to 32
+    assert lib.zg_sgemm_workspace_bytes(4, 8192, 8192, 8192) == 2 * 8192 * 8192 * 4
+    assert lib.zg_sgemm_workspace_bytes(4, 17, 9, 33) == 256 * ((17 * 64 * 4 + 255) // 256) + \
+        256 * ((9 * 64 * 4 + 255) // 256)
     # TF32: the K-major copy of B, plus a pitched copy of A when k % 4 != 0
     assert lib.zg_sgemm_workspace_bytes(2, 64, 64, 64) == 64 * 64 * 4
     assert lib.zg_sgemm_workspace_bytes(2, 17, 9, 33) == 256 * ((17 * 36 * 4 + 255) // 256) + \

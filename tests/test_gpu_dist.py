@@ -88,7 +88,7 @@ def _run(world, **kw):
         assert p.exitcode == 0
 
 
-@pytest.mark.parametrize("mode", [3, 1, 2], ids=["TF32_BF16X2", "TF32X3", "TF32"])
+@pytest.mark.parametrize("mode", [3, 1, 2, 4], ids=["TF32_BF16X2", "TF32X3", "TF32", "BF16X3"])
 def test_chained_gemm_two_ranks(mode):
     # 2 x 1024 rows: 128 x 256 tiles (single-CTA kernel); chunks of 256 columns
     _run(2, mode=mode, m_total=2048, n=4096, k=1024, chunk=256)

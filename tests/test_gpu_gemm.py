@@ -1,6 +1,7 @@
-"""f32 GEMM (SIMT, 3xTF32, TF32) and the fused bias+ReLU epilogue on the
-B200 against the oracle.  Tolerances (relative Frobenius error): SIMT and
-TF32X3 <= 1e-5, TF32 <= 5e-3; the integer KATs are exact in every mode."""
+"""f32 GEMM (SIMT, 3xTF32, TF32, the two bf16-assisted splits) and the fused
+bias+ReLU epilogue on the B200 against the oracle.  Tolerances (relative
+Frobenius error): SIMT, TF32X3, TF32_BF16X2 and BF16X3 <= 1e-5, TF32 <= 5e-3;
+the integer KATs are exact in every mode."""
 from __future__ import annotations
 
 import numpy as np
@@ -13,9 +14,10 @@ from zengpu_b200 import kernels as K
 
 pytestmark = pytest.mark.gpu
 
-MODES = [zg.GemmMode.SIMT_FP32, zg.GemmMode.TF32X3, zg.GemmMode.TF32, zg.GemmMode.TF32_BF16X2]
+MODES = [zg.GemmMode.SIMT_FP32, zg.GemmMode.TF32X3, zg.GemmMode.TF32, zg.GemmMode.TF32_BF16X2,
+         zg.GemmMode.BF16X3]
 TOL = {zg.GemmMode.SIMT_FP32: 1e-5, zg.GemmMode.TF32X3: 1e-5, zg.GemmMode.TF32: 5e-3,
-       zg.GemmMode.TF32_BF16X2: 1e-5}
+       zg.GemmMode.TF32_BF16X2: 1e-5, zg.GemmMode.BF16X3: 1e-5}
 
 
 def bits(x) -> np.ndarray:

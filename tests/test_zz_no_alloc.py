@@ -23,7 +23,7 @@ from zengpu_b200 import kernels as K
 pytestmark = pytest.mark.gpu
 
 TOL = {zg.GemmMode.SIMT_FP32: 1e-5, zg.GemmMode.TF32X3: 1e-5, zg.GemmMode.TF32: 5e-3,
-       zg.GemmMode.TF32_BF16X2: 1e-5}
+       zg.GemmMode.TF32_BF16X2: 1e-5, zg.GemmMode.BF16X3: 1e-5}
 
 
 def _noalloc(a, b, c, mode, alpha=1.0, bias=None, relu=False) -> int:

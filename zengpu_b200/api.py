@@ -103,6 +103,7 @@ class GemmMode(enum.IntEnum):
     TF32X3 = 1
     TF32 = 2
     TF32_BF16X2 = 3
+    BF16X3 = 4
 
 
 class ShaderKind(enum.IntEnum):

@@ -133,7 +133,8 @@ extern "C" int zg_bchain_create(int mode, int k, int n, int chunk_cols, zg_bchai
                                 uint8_t* handle) {
     if (!out || !handle) return set_error(ZG_ERR_DISPATCH, "bchain_create: null output");
     *out = nullptr;
-    if (mode != ZG_GEMM_TF32 && mode != ZG_GEMM_TF32X3 && mode != ZG_GEMM_TF32_BF16X2)
+    if (mode != ZG_GEMM_TF32 && mode != ZG_GEMM_TF32X3 && mode != ZG_GEMM_TF32_BF16X2 &&
+        mode != ZG_GEMM_BF16X3)
         return set_error(ZG_ERR_DISPATCH, "bchain_create: mode %d has no chunked B^T form", mode);
     if (k <= 0 || n <= 0 || chunk_cols <= 0 || chunk_cols % 256 != 0)
         return set_error(ZG_ERR_DISPATCH,

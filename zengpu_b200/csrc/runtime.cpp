@@ -248,6 +248,7 @@ int default_gemm_mode() {
     if (s == "simt" || s == "simt_fp32" || s == "fp32") return ZG_GEMM_SIMT_FP32;
     if (s == "tf32") return ZG_GEMM_TF32;
     if (s == "tf32bf16" || s == "tf32_bf16x2") return ZG_GEMM_TF32_BF16X2;
+    if (s == "bf16x3") return ZG_GEMM_BF16X3;
     return ZG_GEMM_TF32X3;
 }
 
@@ -812,6 +813,7 @@ extern "C" int zg_pipeline_create(zg_device* dev, zg_handle shader, const char* 
             {"sgemm_f32.tf32x3", kSgemmF32, ZG_GEMM_TF32X3},
             {"sgemm_f32.tf32", kSgemmF32, ZG_GEMM_TF32},
             {"sgemm_f32.tf32bf16", kSgemmF32, ZG_GEMM_TF32_BF16X2},
+            {"sgemm_f32.bf16x3", kSgemmF32, ZG_GEMM_BF16X3},
             {"sgemm_bias_relu_f32", kSgemmBiasReluF32, -1},
         };
         for (auto& t : table)
@@ -1370,7 +1372,7 @@ extern "C" int zg_gemm_sgemm_host(const zg_gemm_kernel* kern, zg_device* dev, fl
     if (!c || (k > 0 && (!a || !b))) return set_error(ZG_ERR_DISPATCH, "sgemm_host: null host pointer");
     const int mode = kern->mode;
     if (mode != ZG_GEMM_SIMT_FP32 && mode != ZG_GEMM_TF32X3 && mode != ZG_GEMM_TF32 &&
-        mode != ZG_GEMM_TF32_BF16X2)
+        mode != ZG_GEMM_TF32_BF16X2 && mode != ZG_GEMM_BF16X3)
         return set_error(ZG_ERR_DISPATCH, "sgemm: unknown mode %d", mode);
     std::lock_guard<std::recursive_mutex> lk(dev->mu);
     int rc = set_device(dev);

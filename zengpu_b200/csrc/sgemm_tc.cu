@@ -75,7 +75,7 @@ constexpr uint32_t kTmemCols = 512;              // two BN-column accumulators
 // values of k: 32 f32 for TF32, 16 interleaved split values otherwise).
 template <int S>
 struct TcCfg {
-    static constexpr int BK = S == 1 ? 32 : 16;  // k per stage
+    static constexpr int BK = (S == 1 || S == 4) ? 32 : 16;  // k per stage
     static constexpr int STAGES = 4;
     static constexpr int ROW = 128;              // bytes per operand row per stage
     static constexpr int A_BYTES = BM * ROW;
@@ -134,6 +134,19 @@ __device__ __forceinline__ void issue_stage(uint32_t d_tmem, uint32_t stage_base
     const uint32_t a = stage_base, b = stage_base + Cfg::A_BYTES;
     auto d = [](uint32_t addr) { return umma_desc(addr, 16, 1024, 2); };
     uint32_t acc = first ? 0u : 1u;
+    if (S == 4) {
+        // BF16X3: per 16 of k (32 bytes of the row) lo*hi, hi*lo, then hi*hi;
+        // hi at +0 / +32, lo at +64 / +96
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            const uint32_t ko = kk * 32;
+            mma_f16_ss(d_tmem, d(a + 64 + ko), d(b + ko), kIdescBf16, acc);
+            acc = 1u;
+            mma_f16_ss(d_tmem, d(a + ko), d(b + 64 + ko), kIdescBf16, 1u);
+            mma_f16_ss(d_tmem, d(a + ko), d(b + ko), kIdescBf16, 1u);
+        }
+        return;
+    }
     if (S == 3) {
         // bf16 corrections first (small terms into the accumulator first),
         // one K = 16 MMA each covering the whole stage
@@ -362,7 +375,7 @@ constexpr int PBM = 256, PBN = 256;
 
 template <int S>
 struct PairCfg {
-    static constexpr int BK = S == 1 ? 32 : 16;
+    static constexpr int BK = (S == 1 || S == 4) ? 32 : 16;
     static constexpr int STAGES = 6;
     static constexpr int A_BYTES = 128 * 128;  // this CTA's 128 rows x 128 B
     static constexpr int B_BYTES = 128 * 128;
@@ -382,6 +395,17 @@ __device__ __forceinline__ void issue_stage_pair(uint32_t d_tmem, uint32_t stage
     const uint32_t a = stage_base, b = stage_base + PairCfg<S>::A_BYTES;
     auto d = [](uint32_t addr) { return umma_desc(addr, 16, 1024, 2); };
     uint32_t acc = first ? 0u : 1u;
+    if (S == 4) {
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            const uint32_t ko = kk * 32;
+            mma_f16_ss_pair(d_tmem, d(a + 64 + ko), d(b + ko), kIdescBf16Pair, acc);
+            acc = 1u;
+            mma_f16_ss_pair(d_tmem, d(a + ko), d(b + 64 + ko), kIdescBf16Pair, 1u);
+            mma_f16_ss_pair(d_tmem, d(a + ko), d(b + ko), kIdescBf16Pair, 1u);
+        }
+        return;
+    }
     if (S == 3) {
         mma_f16_ss_pair(d_tmem, d(a + 96), d(b + 64), kIdescBf16Pair, acc);
         acc = 1u;
@@ -605,12 +629,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
 // TF32X3 (S = 2): block kb = k / 16 holds tf32(x) at [kb*32 + j] and
 // tf32(x - hi) at [kb*32 + 16 + j]; TF32_BF16X2 (S = 3): tf32(x) at
 // [kb*32 + j], then 16 bf16(hi) and 16 bf16(x - hi) in the block's last
-// 64 bytes.  j = k % 16.  x = 0 for padding k, so the padding is zero.
+// 64 bytes.  j = k % 16.  BF16X3 (S = 4): 32-k blocks of 32 bf16(x) then 32
+// bf16(x - hi).  x = 0 for padding k, so the padding is zero.
 template <int S>
 __device__ __forceinline__ void put_value(float* base, int64_t ld, int64_t r, int k, float x) {
     float* row = base + r * ld;
     if (S == 1) {
         row[k] = x;
+        return;
+    }
+    if (S == 4) {
+        // BF16X3: block kb = k / 32 holds bf16(x) at bf16 index j and
+        // bf16(x - hi) at 32 + j, j = k % 32
+        const __nv_bfloat16 h = __float2bfloat16_rn(x);
+        const float l = __fsub_rn(x, __bfloat162float(h));  // exact
+        __nv_bfloat16* bb = reinterpret_cast<__nv_bfloat16*>(row + (k >> 5) * 32);
+        bb[k & 31] = h;
+        bb[32 + (k & 31)] = __float2bfloat16_rn(l);
         return;
     }
     const float h = to_tf32(x);
@@ -633,6 +668,24 @@ __device__ __forceinline__ void put_value4(float* base, int64_t ld, int64_t r, i
     float* row = base + r * ld;
     if (S == 1) {
         *reinterpret_cast<float4*>(row + k) = x;
+        return;
+    }
+    if (S == 4) {
+        const float xs[4] = {x.x, x.y, x.z, x.w};
+        float hf[4], lf[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            hf[u] = __bfloat162float(__float2bfloat16_rn(xs[u]));
+            lf[u] = __fsub_rn(xs[u], hf[u]);
+        }
+        __nv_bfloat162 bh[2] = {__floats2bfloat162_rn(hf[0], hf[1]),
+                                __floats2bfloat162_rn(hf[2], hf[3])};
+        __nv_bfloat162 bl[2] = {__floats2bfloat162_rn(lf[0], lf[1]),
+                                __floats2bfloat162_rn(lf[2], lf[3])};
+        __nv_bfloat16* bb = reinterpret_cast<__nv_bfloat16*>(row + (k >> 5) * 32);
+        const int j = k & 31;
+        *reinterpret_cast<uint2*>(bb + j) = *reinterpret_cast<uint2*>(bh);
+        *reinterpret_cast<uint2*>(bb + 32 + j) = *reinterpret_cast<uint2*>(bl);
         return;
     }
     const float xs[4] = {x.x, x.y, x.z, x.w};
@@ -818,22 +871,26 @@ unsigned row_grid(int rows) {
 
 bool valid_mode(int mode) {
     return mode == ZG_GEMM_SIMT_FP32 || mode == ZG_GEMM_TF32X3 || mode == ZG_GEMM_TF32 ||
-           mode == ZG_GEMM_TF32_BF16X2;
+           mode == ZG_GEMM_TF32_BF16X2 || mode == ZG_GEMM_BF16X3;
 }
 
 // Kernel scheme of a tensor-core mode (0: SIMT).
 int scheme_of(int mode) {
     return mode == ZG_GEMM_TF32 ? 1 : mode == ZG_GEMM_TF32X3 ? 2
-                                  : mode == ZG_GEMM_TF32_BF16X2 ? 3 : 0;
+                                  : mode == ZG_GEMM_TF32_BF16X2 ? 3
+                                  : mode == ZG_GEMM_BF16X3 ? 4 : 0;
 }
 
 // k values stored per row of a prepared operand and its pitch (4-byte units).
 int64_t view_kpad(int mode, int K) {
-    return scheme_of(mode) == 1 ? static_cast<int64_t>(round_up(K, 4))
-                                : static_cast<int64_t>(round_up(K, 16));
+    const int sch = scheme_of(mode);
+    return sch == 1 ? static_cast<int64_t>(round_up(K, 4))
+                    : static_cast<int64_t>(round_up(K, sch == 4 ? 32 : 16));
 }
+// TF32: one f32 per k; TF32X3 / TF32_BF16X2: 8 bytes per k; BF16X3: 4.
 int64_t view_pitch(int mode, int K) {
-    return scheme_of(mode) == 1 ? view_kpad(mode, K) : view_kpad(mode, K) * 2;
+    const int sch = scheme_of(mode);
+    return (sch == 1 || sch == 4) ? view_kpad(mode, K) : view_kpad(mode, K) * 2;
 }
 // 4-byte units of the global inner dimension the tensor map covers.
 uint64_t map_cols(int mode, int K) {
@@ -851,6 +908,7 @@ int launch_prep_rows(int mode, const float* src, int rows, int K, int64_t lds,
         case 1: prep_rows_kernel<1><<<grid, 256, 0, s>>>(src, rows, K, lds, dst, v.ld, kpad, vec); break;
         case 2: prep_rows_kernel<2><<<grid, 256, 0, s>>>(src, rows, K, lds, dst, v.ld, kpad, vec); break;
         case 3: prep_rows_kernel<3><<<grid, 256, 0, s>>>(src, rows, K, lds, dst, v.ld, kpad, vec); break;
+        case 4: prep_rows_kernel<4><<<grid, 256, 0, s>>>(src, rows, K, lds, dst, v.ld, kpad, vec); break;
         default: return set_error(ZG_ERR_DISPATCH, "sgemm pre-pass: no planes for mode %d", mode);
     }
     return cuda_status(cudaGetLastError(), "sgemm split pre-pass");
@@ -867,6 +925,7 @@ int launch_prep_transpose(int mode, const float* src, int K, int N, int64_t lds,
         case 1: prep_transpose_kernel<1><<<grid, 256, 0, s>>>(src, K, N, lds, dst, v.ld, kpad); break;
         case 2: prep_transpose_kernel<2><<<grid, 256, 0, s>>>(src, K, N, lds, dst, v.ld, kpad); break;
         case 3: prep_transpose_kernel<3><<<grid, 256, 0, s>>>(src, K, N, lds, dst, v.ld, kpad); break;
+        case 4: prep_transpose_kernel<4><<<grid, 256, 0, s>>>(src, K, N, lds, dst, v.ld, kpad); break;
         default: return set_error(ZG_ERR_DISPATCH, "sgemm pre-pass: no planes for mode %d", mode);
     }
     return cuda_status(cudaGetLastError(), "sgemm transpose pre-pass");
@@ -887,6 +946,7 @@ int launch_prep_transpose_signal(int mode, const float* src, int K, int N, int64
         case 1: prep_transpose_signal_kernel<1><<<grid, 256, 0, s>>>(src, K, N, lds, dst, v.ld, kpad, chunk_cols, counters, flags, epoch); break;
         case 2: prep_transpose_signal_kernel<2><<<grid, 256, 0, s>>>(src, K, N, lds, dst, v.ld, kpad, chunk_cols, counters, flags, epoch); break;
         case 3: prep_transpose_signal_kernel<3><<<grid, 256, 0, s>>>(src, K, N, lds, dst, v.ld, kpad, chunk_cols, counters, flags, epoch); break;
+        case 4: prep_transpose_signal_kernel<4><<<grid, 256, 0, s>>>(src, K, N, lds, dst, v.ld, kpad, chunk_cols, counters, flags, epoch); break;
         default: return set_error(ZG_ERR_DISPATCH, "sgemm pre-pass: no planes for mode %d", mode);
     }
     return cuda_status(cudaGetLastError(), "sgemm chunked transpose pre-pass");
@@ -980,7 +1040,7 @@ int run_tc(const GemmOperands& op, int M, int N, int K, float alpha, float* C, i
 
 // ---- GEMM building blocks (shared with the packed API and the host GEMM) -----------
 bool gemm_a_needs_planes(int mode, int K) {
-    return mode == ZG_GEMM_TF32X3 || mode == ZG_GEMM_TF32_BF16X2 ||
+    return mode == ZG_GEMM_TF32X3 || mode == ZG_GEMM_TF32_BF16X2 || mode == ZG_GEMM_BF16X3 ||
            (mode == ZG_GEMM_TF32 && K % 4 != 0);
 }
 bool gemm_b_needs_planes(int mode) { return scheme_of(mode) > 0; }
@@ -1047,6 +1107,7 @@ int gemm_run(const GemmOperands& op, int M, int N, int K, float alpha, float* C,
         case ZG_GEMM_TF32X3: return run_tc<2>(op, M, N, K, alpha, C, ldc, bias, relu, s, gate);
         case ZG_GEMM_TF32_BF16X2:
             return run_tc<3>(op, M, N, K, alpha, C, ldc, bias, relu, s, gate);
+        case ZG_GEMM_BF16X3: return run_tc<4>(op, M, N, K, alpha, C, ldc, bias, relu, s, gate);
         default: return set_error(ZG_ERR_DISPATCH, "sgemm: unknown mode %d", op.mode);
     }
 }

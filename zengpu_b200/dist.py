@@ -204,7 +204,7 @@ class ChainedGemm:
         self.group, self.src, self.mode, self.k, self.n = group, src, int(mode), k, n
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
-        bpe = 4 if self.mode == 2 else 8
+        bpe = 4 if self.mode in (2, 4) else 8  # packed bytes per element of B
         self.chunk_cols = chunk_cols or default_chunk_cols(n, k, bytes_per_elem=bpe)
         self.chunks = (n + self.chunk_cols - 1) // self.chunk_cols
         self.prev, self.next = chain_neighbours(self.rank, self.world, src)

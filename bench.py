@@ -50,6 +50,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 #   --section MemoryWorkloadAnalysis -k regex:stream_vec_kernel on the elementwise workload
 # Keyed by the kernel and the per-rank GEMM size (M = N = K) or element count.
 NCU_TRAFFIC = {
+    ("sgemm_tc_pair_kernel<4>", 8192): 4.179e9,
     ("sgemm_tc_pair_kernel<3>", 8192): 5.642e9,
     ("sgemm_tc_pair_kernel<2>", 8192): 5.999e9,
     ("sgemm_tc_kernel<3>", 8192): 4.841e9,
@@ -505,7 +506,8 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
                                    f"dp{world} (A/C row blocks, B broadcast over NCCL in "
                                    f"{panels} column panels)" if world > 1 else
                                    "dp1 (one GPU, no exchange)"),
-                   "l2": "inputs larger than L2: A, B 256 MiB each, plus 1 GiB of hi/lo planes"},
+                   "l2": f"inputs larger than L2: A {m_local * k * 4 >> 20} MiB, B {k * n * 4 >> 20} MiB, "
+                         f"packed operands {algorithmic_bytes(mode, m_local, n, k) - 4 * m_local * n >> 20} MiB"},
         "roofline": {"bound": "tensor" if mode != zg.GemmMode.SIMT_FP32 else "fp32",
                      "kernel": tc_kernel_name(torch, int(mode), m_local, n),
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
@@ -861,9 +863,9 @@ def mlp_workload(args, torch, zg, K, mode, peaks, peak_src, world):
         "config": {"workload": f"op_graph_lower MLP 4 x relu(X@W+b), 4096x4096, {args.mode}",
                    "unfused_ms_per_step": res["unfused"],
                    "speedup_fused_vs_unfused": res["unfused"] / res["fused"]},
-        # per layer: TF32X3 / TF32_BF16X2 pack A, pack B, kernel; TF32 transpose B,
+        # per layer: TF32X3 / TF32_BF16X2 / BF16X3 pack A, pack B, kernel; TF32 transpose B,
         # kernel; SIMT one kernel
-        "gpu_launches": args.steps * layers * {1: 3, 2: 2, 3: 3}.get(int(mode), 1),
+        "gpu_launches": args.steps * layers * {1: 3, 2: 2, 3: 3, 4: 3}.get(int(mode), 1),
         "clocks": clock_summary,
     }
 

@@ -733,53 +733,73 @@ __global__ void __launch_bounds__(256)
     }
 }
 
-// Transposing pre-pass for B: view row n, k from a K x N source (pitch lds),
-// through a 32 x 33 shared tile so both reads and writes are coalesced;
-// k in [K, kpad) written as zero.
+// Transposing pre-pass for B: view row n, k from a K x N source (pitch lds).
+// A CTA takes a 32-column strip of B over kTransposeTiles tiles of 64 k
+// (blockIdx.x = group of k tiles, blockIdx.y = strip): each tile passes
+// through a 64 x 33 shared tile so reads and writes are both coalesced.  Each
+// thread keeps eight loads in flight, and the next tile's loads are issued
+// before the current tile is stored (the shared tile is double buffered, one
+// barrier per tile).  k in [K, kpad) is written as zero.
+constexpr int kTransposeTileK = 64;
+constexpr int kTransposeTiles = 4;
+
+template <int S>
+__device__ __forceinline__ void transpose_strip(const float* __restrict__ src, int K, int N,
+                                                int64_t lds, float* dst, int64_t ldd, int kpad,
+                                                int n0, int kt0, int kt1) {
+    constexpr int TK = kTransposeTileK;
+    __shared__ float tile[2][TK][33];
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    float r[TK / 8];
+    auto load = [&](int kt) {
+#pragma unroll
+        for (int j = 0; j < TK / 8; ++j) {
+            const int k = kt * TK + ty + 8 * j, n = n0 + tx;
+            r[j] = (k < K && n < N) ? __ldcs(src + static_cast<int64_t>(k) * lds + n) : 0.f;
+        }
+    };
+    if (kt0 < kt1) load(kt0);
+    for (int kt = kt0; kt < kt1; ++kt) {
+        const int b = (kt - kt0) & 1;
+#pragma unroll
+        for (int j = 0; j < TK / 8; ++j) tile[b][ty + 8 * j][tx] = r[j];
+        __syncthreads();
+        if (kt + 1 < kt1) load(kt + 1);
+        // 32 rows n x 64 k: warp ty stores rows ty, ty + 8, ..., each in two 32-k halves
+#pragma unroll
+        for (int j = 0; j < TK / 8; ++j) {
+            const int nl = ty + 8 * (j >> 1), kl = (j & 1) * 32 + tx;
+            const int n = n0 + nl, k = kt * TK + kl;
+            if (n < N && k < kpad) put_value<S>(dst, ldd, n, k, tile[b][kl][nl]);
+        }
+    }
+}
+
 template <int S>
 __global__ void __launch_bounds__(256)
     prep_transpose_kernel(const float* __restrict__ src, int K, int N, int64_t lds, float* dst,
                           int64_t ldd, int kpad) {
-    __shared__ float tile[32][33];
-    const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-#pragma unroll
-    for (int j = ty; j < 32; j += 8) {
-        const int k = k0 + j, n = n0 + tx;
-        tile[j][tx] = (k < K && n < N) ? __ldcs(src + static_cast<int64_t>(k) * lds + n) : 0.f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int j = ty; j < 32; j += 8) {
-        const int n = n0 + j, k = k0 + tx;
-        if (n < N && k < kpad) put_value<S>(dst, ldd, n, k, tile[tx][j]);
-    }
+    const int kt_total = (kpad + kTransposeTileK - 1) / kTransposeTileK;
+    const int kt0 = blockIdx.x * kTransposeTiles;
+    transpose_strip<S>(src, K, N, lds, dst, ldd, kpad, blockIdx.y * 32, kt0,
+                       min(kt_total, kt0 + kTransposeTiles));
 }
 
-// The transpose pre-pass of B for a chunked hand-off: CTAs run k-block
-// fastest, so column strips (and chunks of chunk_cols columns) finish in
-// order, and the last CTA of chunk c publishes flags[c] = epoch with a
-// system-scope release (the copy engine and other GPUs read the chunk after
-// seeing it).  counters[] (one per chunk) start at zero.
+// The transpose pre-pass for a chunked hand-off: the k-tile groups of a strip
+// are the fastest grid dimension, so column strips (and chunks of chunk_cols
+// columns) finish in order, and the last CTA of chunk c publishes flags[c] =
+// epoch with a system-scope release (the copy engine and other GPUs read the
+// chunk after seeing it).  counters[] (one per chunk) start at zero.
 template <int S>
 __global__ void __launch_bounds__(256)
     prep_transpose_signal_kernel(const float* __restrict__ src, int K, int N, int64_t lds,
                                  float* dst, int64_t ldd, int kpad, int chunk_cols,
                                  uint32_t* counters, uint32_t* flags, uint32_t epoch) {
-    __shared__ float tile[32][33];
-    const int k0 = blockIdx.x * 32, n0 = blockIdx.y * 32;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-#pragma unroll
-    for (int j = ty; j < 32; j += 8) {
-        const int k = k0 + j, n = n0 + tx;
-        tile[j][tx] = (k < K && n < N) ? __ldcs(src + static_cast<int64_t>(k) * lds + n) : 0.f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int j = ty; j < 32; j += 8) {
-        const int n = n0 + j, k = k0 + tx;
-        if (n < N && k < kpad) put_value<S>(dst, ldd, n, k, tile[tx][j]);
-    }
+    const int kt_total = (kpad + kTransposeTileK - 1) / kTransposeTileK;
+    const int kt0 = blockIdx.x * kTransposeTiles;
+    const int n0 = blockIdx.y * 32;
+    transpose_strip<S>(src, K, N, lds, dst, ldd, kpad, n0, kt0,
+                       min(kt_total, kt0 + kTransposeTiles));
     __threadfence();  // this thread's part of the chunk, before the CTA is counted
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -918,8 +938,10 @@ int launch_prep_transpose(int mode, const float* src, int K, int N, int64_t lds,
                           const OperandView& v, cudaStream_t s) {
     if (K == 0 || N == 0) return ZG_OK;
     const int kpad = static_cast<int>(view_kpad(mode, K));
-    dim3 grid((N + 31) / 32, (kpad + 31) / 32);
-    if (grid.y > 65535u) return set_error(ZG_ERR_DISPATCH, "sgemm: k too large for the pre-pass");
+    const int kgroups =
+        ((kpad + kTransposeTileK - 1) / kTransposeTileK + kTransposeTiles - 1) / kTransposeTiles;
+    dim3 grid(kgroups, (N + 31) / 32);
+    if (grid.y > 65535u) return set_error(ZG_ERR_DISPATCH, "sgemm: n too large for the pre-pass");
     float* dst = static_cast<float*>(v.p);
     switch (scheme_of(mode)) {
         case 1: prep_transpose_kernel<1><<<grid, 256, 0, s>>>(src, K, N, lds, dst, v.ld, kpad); break;
@@ -937,7 +959,9 @@ int launch_prep_transpose_signal(int mode, const float* src, int K, int N, int64
     if (K == 0 || N == 0) return ZG_OK;
     const int kpad = static_cast<int>(view_kpad(mode, K));
     const int chunks = (N + chunk_cols - 1) / chunk_cols;
-    dim3 grid((kpad + 31) / 32, (N + 31) / 32);
+    const int kgroups =
+        ((kpad + kTransposeTileK - 1) / kTransposeTileK + kTransposeTiles - 1) / kTransposeTiles;
+    dim3 grid(kgroups, (N + 31) / 32);
     if (grid.y > 65535u) return set_error(ZG_ERR_DISPATCH, "sgemm: n too large for the pre-pass");
     cudaError_t e = cudaMemsetAsync(counters, 0, static_cast<size_t>(chunks) * sizeof(uint32_t), s);
     if (e != cudaSuccess) return cuda_status(e, "sgemm chunked pre-pass: counters");

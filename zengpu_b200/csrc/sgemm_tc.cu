@@ -307,8 +307,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
             for (int j = 0; j < nchunks; ++j, ++cj) {
                 const int buf = cj & 1;
-                if (!mbar_wait_bounded(&acc_full[buf], (cj >> 1) & 1, &g_status,
-                                       kErrTcEpilogue)) {
+                // the whole warp gives up together: the TMEM loads below are
+                // warp-collective, so no lane may go on alone
+                const bool got = mbar_wait_bounded(&acc_full[buf], (cj >> 1) & 1, &g_status,
+                                                   kErrTcEpilogue);
+                if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
                     break;
                 }
@@ -569,8 +572,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
             for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
             for (int j = 0; j < nchunks; ++j, ++cj) {
                 const int buf = cj & 1;
-                if (!mbar_wait_bounded(&acc_full[buf], (cj >> 1) & 1, &g_status,
-                                       kErrTcEpilogue)) {
+                // the whole warp gives up together: the TMEM loads below are
+                // warp-collective, so no lane may go on alone
+                const bool got = mbar_wait_bounded(&acc_full[buf], (cj >> 1) & 1, &g_status,
+                                                   kErrTcEpilogue);
+                if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
                     break;
                 }

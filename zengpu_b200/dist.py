@@ -242,15 +242,18 @@ class ChainedGemm:
         m = a_rows.shape[0]
         if tuple(out.shape) != (m, self.n) or out.stride(1) != 1:
             raise ValueError(f"ChainedGemm: out must be [{m}, {self.n}] with unit column stride")
+        is_src = self.rank == self.src
+        if is_src and (b is None or tuple(b.shape) != (self.k, self.n) or b.stride(1) != 1):
+            raise ValueError(f"ChainedGemm: the source rank needs B [{self.k}, {self.n}]")
+        if bias is not None and (bias.numel() != self.n or not bias.is_contiguous()):
+            raise ValueError(f"ChainedGemm: bias must be a contiguous [{self.n}] vector")
+        # every check is done: from here on each rank enqueues the same step e
         self.epoch += 1
         e = self.epoch & 0xFFFFFFFF
         compute = torch.cuda.current_stream()
         cs = C.c_void_p(compute.cuda_stream)
         copy = C.c_void_p(self.copy_stream.cuda_stream)
-        is_src = self.rank == self.src
         if is_src:
-            if b is None or tuple(b.shape) != (self.k, self.n) or b.stride(1) != 1:
-                raise ValueError(f"ChainedGemm: the source rank needs B [{self.k}, {self.n}]")
             # packs chunk by chunk; each chunk's flag lets the copy stream push it on
             self._check(self.lib.zg_bchain_source(self.chain, e, b.data_ptr(), b.stride(0), cs))
         self._check(self.lib.zg_bchain_forward(self.chain, e, copy))

@@ -2,7 +2,7 @@
 // dispatcher behind zg_sgemm_f32 (the kernel contract of GEMM_PTX's entry
 // `main(a, b, c, m, n, k, alpha)`, zengpu-blas/src/level3.rs:35-90).
 //
-// Three tensor-core modes share one kernel template (S = planes per operand):
+// Four tensor-core modes share one kernel template (S = operand scheme):
 //   TF32 (S=1)         one kind::tf32 MMA per k-step on f32 operands;
 //   TF32X3 (S=2)       split precision: x = hi + lo, hi = tf32(x),
 //                      lo = tf32(x - hi) (round to nearest both);
@@ -12,14 +12,20 @@
 //                      only need ~2^-19 relative precision, run as one
 //                      kind::f16 bf16 MMA each (twice the tf32 rate):
 //                      D += bf16(A_lo)*bf16(B_hi) + bf16(A_hi)*bf16(B_lo)
-//                         + A_hi*B_hi (tf32): 2/3 of TF32X3's MMA time.
+//                         + A_hi*B_hi (tf32): 2/3 of TF32X3's MMA time;
+//   BF16X3 (S=4)       x = hi + lo with hi = bf16(x), lo = bf16(x - hi);
+//                      D += A_lo*B_hi + A_hi*B_lo + A_hi*B_hi as three
+//                      kind::f16 bf16 MMAs (products exact in f32; the
+//                      dropped lo*lo and the residue below lo are ~2^-16):
+//                      1/2 of TF32X3's MMA time and half its operand bytes.
 // A pre-pass writes the operands in the layout the kernel reads: A with k
-// innermost, B transposed to K-major, and for the split modes every 16-k block
-// of a row packed into one 128-byte row holding all of that block's terms
-// (TF32X3: 16 tf32 hi | 16 tf32 lo; TF32_BF16X2: 16 tf32 hi | 16 bf16 hi |
-// 16 bf16 lo).  Full 128-byte rows keep the TMA engine at full rate: one box
-// per operand per stage, one 128-byte swizzle for every term, and each MMA
-// descriptor is an offset into the same swizzled rows.
+// innermost, B transposed to K-major, and for the split modes every block of
+// k of a row packed into one 128-byte row holding all of that block's terms
+// (TF32X3, 16 k: 16 tf32 hi | 16 tf32 lo; TF32_BF16X2, 16 k: 16 tf32 hi | 16
+// bf16 hi | 16 bf16 lo; BF16X3, 32 k: 32 bf16 hi | 32 bf16 lo).  Full
+// 128-byte rows keep the TMA engine at full rate: one box per operand per
+// stage, one 128-byte swizzle for every term, and each MMA descriptor is an
+// offset into the same swizzled rows.
 //
 // Kernel layout (persistent, one CTA per SM, 128 x 256 output tiles, 320
 // threads):
@@ -38,9 +44,14 @@
 //               applies alpha / bias / ReLU and stores with 128-bit writes.
 //               The chunk pipeline runs on across tiles, so a tile's final
 //               drain and store overlap the next tile's MMAs.
-// Every mbarrier wait is bounded (zg_common.cuh); an expiry sets a bit in the
-// device status word, the kernel drains its in-flight copies and MMAs, frees
-// TMEM and returns.
+// Problems with a 256 x 256 tile for every SM pair run the CTA-pair variant
+// (sgemm_tc_pair_kernel: tcgen05 cta_group::2, M = 256, six 32 KB stages per
+// CTA).  A GemmGate lets a GEMM start while its B^T rows are still arriving
+// from another GPU: the producer waits for the chunk flag of each tile's B
+// rows before loading them.
+// Every mbarrier and flag wait is bounded (zg_common.cuh); an expiry sets a
+// bit in the device status word, the kernel drains its in-flight copies and
+// MMAs, frees TMEM and returns.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>

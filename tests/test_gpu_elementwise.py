@@ -1,9 +1,9 @@
 """DeviceArray add / ReLU / Level-1 on the B200 against the oracle: bit-exact.
 
 Mirrors zengpu-conformance/tests/devarray_elementwise.rs (KATs through the
-ElementwiseKernels + BufferPool API), then seeded parity at the BASELINE
-sizes (256x256 and 2^28), the edge sizes of the float4 path and the pinned
-ReLU semantics."""
+ElementwiseKernels + BufferPool API), then seeded parity at the workload
+sizes (256x256 and 2^28 elements), the edge sizes of the float4 path and the
+pinned ReLU semantics."""
 from __future__ import annotations
 
 import numpy as np

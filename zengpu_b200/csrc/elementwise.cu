@@ -4,8 +4,9 @@
 // seeded input generators.
 //
 // Each kernel is grid-stride over 16-byte float4 lanes with streaming cache
-// hints (the data is touched once), UNROLL independent loads in flight per
-// thread, and a scalar tail.  Arithmetic is plain IEEE f32 with no
+// hints (the data is touched once), eight independent 16-byte loads in flight
+// per thread (four from each input for binary ops, eight from the one input
+// for unary ops), and a scalar tail.  Arithmetic is plain IEEE f32 with no
 // contraction (__fadd_rn / __fmul_rn), so results are bit-identical to the
 // Rust CPU backend.
 #include <cstdint>
@@ -16,7 +17,9 @@ namespace zg {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kUnroll = 4;
+// float4 loads in flight per thread and input: 128 bytes per thread either way
+template <bool kBinary>
+constexpr int kUnroll = kBinary ? 4 : 8;
 
 int sm_count() {
     static thread_local int cached_dev = -1, cached = 0;
@@ -72,17 +75,18 @@ __global__ void __launch_bounds__(kThreads)
     stream_vec_kernel(const float4* a, const float4* b, float4* out, uint64_t n4,
                       const float* a_s, const float* b_s, float* out_s, uint32_t tail,
                       float scalar) {
+    constexpr int U = kUnroll<kBinary>;
     const uint64_t stride = static_cast<uint64_t>(gridDim.x) * kThreads;
     uint64_t i = static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
-    for (; i + (kUnroll - 1) * stride < n4; i += kUnroll * stride) {
-        float4 va[kUnroll], vb[kUnroll];
+    for (; i + (U - 1) * stride < n4; i += U * stride) {
+        float4 va[U], vb[U];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
+        for (int u = 0; u < U; ++u) {
             va[u] = ld_stream(a + i + u * stride);
-            if (kBinary) vb[u] = ld_stream(b + i + u * stride);
+            vb[u] = kBinary ? ld_stream(b + i + u * stride) : va[u];
         }
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) __stcs(out + i + u * stride, apply4<Op>(va[u], vb[u], scalar));
+        for (int u = 0; u < U; ++u) __stcs(out + i + u * stride, apply4<Op>(va[u], vb[u], scalar));
     }
     for (; i < n4; i += stride) {
         float4 va = ld_stream(a + i);

@@ -53,6 +53,7 @@ NCU_TRAFFIC = {
     ("sgemm_tc_pair_kernel<4>", 8192): 4.179e9,
     ("sgemm_tc_pair_kernel<3>", 8192): 5.642e9,
     ("sgemm_tc_pair_kernel<2>", 8192): 5.999e9,
+    ("sgemm_tc_pair_kernel<1>", 8192): 3.105e9,
     ("sgemm_tc_kernel<3>", 8192): 4.841e9,
     ("sgemm_tc_kernel<2>", 8192): 4.869e9,
     ("stream_vec_kernel<AddOp>", 1 << 28): 3.188e9,

@@ -1402,9 +1402,11 @@ extern "C" int zg_gemm_sgemm_host(const zg_gemm_kernel* kern, zg_device* dev, fl
     const OperandView b_ps = b_planes ? gemm_carve_planes(base + o_bp, mode, N, K)
                                       : gemm_raw_operand(dB, N);
 
-    // Row panels of A / C: large enough to keep the GEMM efficient, small
-    // enough that uploading A, computing and downloading C overlap.
-    const int rows = M <= 1024 ? M : std::max(512, (((M + 7) / 8 + 127) / 128) * 128);
+    // Row panels of A / C (16, of at least 512 rows): the host links, not the
+    // GEMM, bound this call, so panels only need to keep the GPU busy enough
+    // to hide under the uploads; smaller panels shorten the tail (the last
+    // panel's GEMM and C download) that nothing overlaps.
+    const int rows = M <= 1024 ? M : std::max(512, (((M + 15) / 16 + 127) / 128) * 128);
     const int panels = (M + rows - 1) / rows;
     std::vector<cudaEvent_t> ev(2 * panels + 1, nullptr);
     for (auto& e : ev)

@@ -74,7 +74,7 @@ def env_ranks() -> tuple[int, int, int]:
 
 # ---- clocks -------------------------------------------------------------------------
 class ClockSampler:
-    """SM clock, power and clock-event reasons of one GPU, sampled every 10 ms
+    """SM clock, power and clock-event reasons of one GPU, sampled every 2 ms
     on a background thread while the `with` block (the timed region) runs.
 
     The GPU is found through NVML by the PCI bus id of the CUDA device, so the
@@ -83,7 +83,7 @@ class ClockSampler:
     (sm_mhz, sm_max_mhz, power_w, set of active reason names)."""
 
     REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-    PERIOD_S = 0.010
+    PERIOD_S = 0.002
 
     def __init__(self, cuda_index: int = 0, reader=None):
         self.cuda_index = cuda_index

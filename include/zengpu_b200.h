@@ -402,7 +402,8 @@ int zg_kernel_status(uint32_t *code);
  * Two buffers alternate between steps.  A wait that can never end (a rank
  * that died) is ended by zg_bchain_abort on the waiting ranks; the GEMM's own
  * gate gives up after 2 s and reports ZG_ERR_KERNEL_WAIT through
- * zg_kernel_status.  Tensor-core modes only.  A chain object belongs to the
+ * zg_kernel_status.  After an abort the flags order nothing any more: the
+ * results of the aborted steps are invalid and the chain is only destroyed.  Tensor-core modes only.  A chain object belongs to the
  * device current at create and is driven from one host thread. */
 #define ZG_IPC_HANDLE_BYTES 64
 typedef struct zg_bchain zg_bchain;

@@ -510,10 +510,10 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
                    "l2": f"inputs larger than L2: A {m_local * k * 4 >> 20} MiB, B {k * n * 4 >> 20} MiB, "
                          f"packed operands {algorithmic_bytes(mode, m_local, n, k) - 4 * m_local * n >> 20} MiB"},
         "roofline": {"bound": "tensor" if mode != zg.GemmMode.SIMT_FP32 else "fp32",
-                     "kernel": tc_kernel_name(torch, int(mode), m_local, n),
+                     "kernel": tc_kernel_name(torch, int(mode), m_local, n, k),
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak,
-                     "traffic": NCU_TRAFFIC.get((tc_kernel_name(torch, int(mode), m_local, n), s))
+                     "traffic": NCU_TRAFFIC.get((tc_kernel_name(torch, int(mode), m_local, n, k), s))
                      if args.workload == "gemm" else None,
                      "algorithmic_bytes": algorithmic_bytes(mode, m_local, n, k),
                      "kernel_ms": kern_ms,
@@ -545,17 +545,11 @@ def gemm_workload(args, torch, dist, zg, K, mode, peaks, peak_src, rank, local_r
     return line
 
 
-def tc_kernel_name(torch, mode: int, m: int, n: int) -> str:
-    """The GEMM kernel the library launches for an m x n output (its rule: the
-    CTA-pair kernel once there is a 256 x 256 tile for every SM pair, unless
-    ZENGPU_GEMM_PAIRS=0)."""
-    if mode == 0:
-        return "sgemm_simt_kernel"
-    scheme = {1: 2, 2: 1, 3: 3, 4: 4}[mode]
-    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    pairs = (-(-m // 256)) * (-(-n // 256)) >= sms // 2 and os.environ.get(
-        "ZENGPU_GEMM_PAIRS", "1")[:1] != "0"
-    return f"sgemm_tc_pair_kernel<{scheme}>" if pairs else f"sgemm_tc_kernel<{scheme}>"
+def tc_kernel_name(torch, mode: int, m: int, n: int, k: int = 8192) -> str:
+    """The main GEMM kernel the library launches for this problem, as the
+    library itself reports it."""
+    import zengpu_b200 as zg
+    return zg.load_library().zg_sgemm_kernel_name(int(mode), m, n, k).decode()
 
 
 def sampled_accuracy(torch, dist, a, b, c, mode, world) -> dict:

@@ -374,6 +374,13 @@ int zg_sgemm_f32_noalloc(int mode, int m, int n, int k, float alpha, const float
 int zg_fill_uniform_f32(float *x, uint64_t n, uint64_t seed, float lo, float hi, void *stream);
 int zg_fill_normal_f32(float *x, uint64_t n, uint64_t seed, void *stream);
 
+/* Name of the main kernel zg_sgemm_f32 / zg_sgemm_packed launch for
+ * (mode, m, n, k) on the current device ("" for an unknown mode or an empty
+ * output), for reports and profiler filters.  The tensor-core modes take the
+ * CTA-pair kernel once there is a 256 x 256 tile for every SM pair (unless
+ * the environment sets ZENGPU_GEMM_PAIRS=0). */
+const char *zg_sgemm_kernel_name(int mode, int m, int n, int k);
+
 /* Reads and clears the device-side status word of the current device:
  * *code = 0 when every bounded on-device wait since the last call finished
  * in time, else a bitmask of the kernels whose wait expired.  Synchronises. */

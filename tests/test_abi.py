@@ -124,3 +124,16 @@ def test_bchain_argument_errors_need_no_gpu():
     assert lib.zg_bchain_gemm(None, 1, 1, 8, 1.0, None, None, 512, None, 0, None) == \
         zg.api.Dispatch.code
     assert lib.zg_bchain_destroy(None) == 0
+
+
+def test_sgemm_kernel_name():
+    """The launch rule as the library reports it (148 SMs when no GPU answers)."""
+    lib = zg.load_library()
+    name = lambda *a: lib.zg_sgemm_kernel_name(*a).decode()  # noqa: E731
+    assert name(4, 8192, 8192, 8192) == "sgemm_tc_pair_kernel<4>"
+    assert name(3, 8192, 8192, 8192) == "sgemm_tc_pair_kernel<3>"
+    assert name(1, 256, 512, 64) == "sgemm_tc_kernel<2>"
+    assert name(2, 256, 512, 64) == "sgemm_tc_kernel<1>"
+    assert name(0, 8192, 8192, 8192) == "sgemm_simt_kernel"
+    assert name(3, 64, 64, 0) == "gemm_k0_kernel"
+    assert name(9, 64, 64, 64) == "" and name(3, 0, 64, 64) == ""

@@ -150,6 +150,7 @@ SIGNATURES: dict[str, tuple] = {
     "zg_fill_uniform_f32": (_i, [_fp, _u64, _u64, _f, _f, _vp]),
     "zg_fill_normal_f32": (_i, [_fp, _u64, _u64, _vp]),
     "zg_kernel_status": (_i, [C.POINTER(_u32)]),
+    "zg_sgemm_kernel_name": (C.c_char_p, [_i, _i, _i, _i]),
     "zg_bchain_create": (_i, [_i, _i, _i, _i, C.POINTER(_vp), C.POINTER(C.c_uint8)]),
     "zg_bchain_connect": (_i, [_vp, C.POINTER(C.c_uint8), C.POINTER(C.c_uint8)]),
     "zg_bchain_source": (_i, [_vp, _u32, _fp, C.c_int64, _vp]),

@@ -1332,6 +1332,18 @@ extern "C" int zg_sgemm_packed(int mode, int m, int n, int k, float alpha, const
     return gemm_run(op, m, n, k, alpha, c, ldc, bias, relu, s);
 }
 
+extern "C" const char* zg_sgemm_kernel_name(int mode, int m, int n, int k) {
+    if (!valid_mode(mode) || m <= 0 || n <= 0 || k < 0) return "";
+    if (k == 0) return "gemm_k0_kernel";
+    if (mode == ZG_GEMM_SIMT_FP32) return "sgemm_simt_kernel";
+    static const char* const pair[] = {"", "sgemm_tc_pair_kernel<1>", "sgemm_tc_pair_kernel<2>",
+                                       "sgemm_tc_pair_kernel<3>", "sgemm_tc_pair_kernel<4>"};
+    static const char* const single[] = {"", "sgemm_tc_kernel<1>", "sgemm_tc_kernel<2>",
+                                         "sgemm_tc_kernel<3>", "sgemm_tc_kernel<4>"};
+    const int sch = scheme_of(mode);
+    return use_pairs(m, n) ? pair[sch] : single[sch];
+}
+
 extern "C" int zg_kernel_status(uint32_t* code) {
     uint32_t v = 0, zero = 0;
     cudaError_t e = cudaMemcpyFromSymbol(&v, g_status, sizeof(v));

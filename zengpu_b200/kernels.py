@@ -14,7 +14,9 @@ import torch
 from . import _lib as L
 from .api import GemmMode, check
 
-_workspaces: dict[int, torch.Tensor] = {}
+# One scratch tensor per (device, stream): GEMMs issued on different streams
+# may overlap, and each stream reuses its own scratch in stream order.
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
 
 
 def _stream(t: torch.Tensor) -> C.c_void_p:
@@ -64,14 +66,16 @@ def workspace_bytes(mode: int, m: int, n: int, k: int) -> int:
 
 
 def workspace_for(device: torch.device, nbytes: int) -> torch.Tensor | None:
-    """Per-device scratch tensor, grown on demand (stream-ordered reuse)."""
+    """Scratch tensor of the current stream on `device`, grown on demand
+    (reused in stream order, so only GEMMs on that stream share it)."""
     if nbytes == 0:
         return None
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    ws = _workspaces.get(idx)
+    key = (idx, torch.cuda.current_stream(idx).cuda_stream)
+    ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
-        _workspaces[idx] = ws
+        _workspaces[key] = ws
     return ws
 
 

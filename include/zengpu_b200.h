@@ -115,6 +115,27 @@ typedef struct zg_submission zg_submission;
 
 /* Message of the last failed call on this thread ("" if none). */
 const char *zg_last_error(void);
+
+/* The fields of the last failure on this thread, so a binding can rebuild the
+ * reference's error value exactly (zengpu-hal/src/error.rs:15-58):
+ *   ZG_ERR_STALE_HANDLE     UsageError::StaleHandle { index, expected_gen, actual_gen }
+ *   ZG_ERR_MISSING_USAGE    UsageError::MissingUsage { resource, needed }
+ *                           (static strings, e.g. "buffer" / "READBACK")
+ *   ZG_ERR_OUT_OF_MEMORY    GpuError::OutOfMemory(memory) (ZG_MEMORY_*)
+ *   ZG_ERR_UNSUPPORTED_FEATURES  GpuError::UnsupportedFeatures(features)
+ * Fields a status does not use are zero / "".  status is 0 before any failure. */
+typedef struct zg_error_detail {
+    int32_t status;
+    uint32_t handle_index;
+    uint32_t expected_gen;
+    uint32_t actual_gen;
+    uint32_t memory;
+    uint32_t reserved;
+    uint64_t features;
+    const char *resource;
+    const char *needed;
+} zg_error_detail;
+int zg_last_error_detail(zg_error_detail *out);
 int zg_abi_version(void);
 
 /* Number of CUDA devices; ZG_ERR_NO_DEVICE when the driver cannot init.
@@ -129,8 +150,10 @@ void zg_device_close(zg_device *dev);
 int zg_device_ordinal(const zg_device *dev);
 /* The device's stream (a cudaStream_t), for interop with layer 3. */
 void *zg_device_stream(zg_device *dev);
-/* GpuDevice::can_peer (zengpu-hal/src/device.rs:91-94): 1 if peer access from
- * `peer_ordinal` works, else 0. */
+/* GpuDevice::can_peer (zengpu-hal/src/device.rs:91-94), as the HIP backend
+ * implements it (zengpu-hip/src/lib.rs:613-631): 1 once `dev` can access
+ * `peer_ordinal`'s memory (peer access is enabled on the first query and the
+ * answer cached per peer), else 0; a device can always reach itself. */
 int zg_device_can_peer(zg_device *dev, int peer_ordinal, int *out);
 
 /* GpuDevice::create_buffer (zengpu-cuda/src/lib.rs:481-500). */
@@ -141,6 +164,19 @@ int zg_buffer_write(zg_device *dev, zg_handle buf, uint64_t offset, const void *
                     uint64_t len);
 /* GpuDevice::read_buffer_into (zengpu-cuda/src/lib.rs:560-615): needs READBACK. */
 int zg_buffer_read(zg_device *dev, zg_handle buf, uint64_t offset, void *dst, uint64_t len);
+/* Asynchronous counterpart of zg_buffer_read (new; the reference only has the
+ * synchronous read_buffer_into, zengpu-cuda/src/lib.rs:560-615): queues a
+ * device -> host copy of `len` bytes at `offset` into `dst` on the device
+ * stream, after everything queued before it, and returns a submission whose
+ * poll / wait report completion (like zg_submit_batch's).  Needs READBACK or
+ * TRANSFER_SRC usage, so GpuOnly arrays (no READBACK) read back this way.
+ * `dst` must stay valid and unread until the submission completes; page-locked
+ * host memory makes the copy truly asynchronous.  While the submission is
+ * pending the in-flight rules hold (no synchronous write / read / copy).  If a
+ * GEMM queued before it without a synchronize had a bounded on-device wait
+ * expire, the completing poll / wait returns ZG_ERR_KERNEL_WAIT. */
+int zg_buffer_read_async(zg_device *dev, zg_handle buf, uint64_t offset, void *dst,
+                         uint64_t len, zg_submission **out);
 /* GpuDevice::copy_buffer (zengpu-cuda/src/lib.rs:617-691). */
 int zg_buffer_copy(zg_device *dev, zg_handle src, uint64_t src_offset, zg_handle dst,
                    uint64_t dst_offset, uint64_t len);
@@ -149,7 +185,10 @@ int zg_buffer_copy(zg_device *dev, zg_handle src, uint64_t src_offset, zg_handle
 void zg_buffer_destroy(zg_device *dev, zg_handle buf);
 /* Device address and size of a live buffer (for layer 3 interop). */
 int zg_buffer_info(zg_device *dev, zg_handle buf, uint64_t *device_ptr, uint64_t *size);
-/* GpuDevice::copy_from_peer (zengpu-hal/src/device.rs:96-106) over NVLink. */
+/* GpuDevice::copy_from_peer (zengpu-hal/src/device.rs:96-106; HIP backend
+ * zengpu-hip/src/lib.rs:633-710): `bytes` from src (on src_dev) to dst (on
+ * dst_dev), a direct copy over NVLink when can_peer holds, else staged through
+ * host memory; synchronous.  A size beyond either buffer is ZG_ERR_BACKEND. */
 int zg_buffer_copy_from_peer(zg_device *dst_dev, zg_handle dst, zg_device *src_dev,
                              zg_handle src, uint64_t bytes);
 
@@ -222,8 +261,20 @@ typedef struct zg_pool zg_pool;
 
 /* size_class (zengpu-compute/src/pool.rs:75-78): next pow2, min 256 bytes. */
 uint64_t zg_size_class(uint64_t size);
-/* BufferPool::new / drop (zengpu-compute/src/pool.rs:17-89). */
+/* BufferPool::new / drop (zengpu-compute/src/pool.rs:17-89): Upload
+ * residency, STORAGE | READBACK buffers, as the reference (:47-51). */
 int zg_pool_create(zg_device *dev, zg_pool **out);
+/* BufferPool with a chosen residency (new): ZG_MEMORY_UPLOAD as above, or
+ * ZG_MEMORY_GPU_ONLY for device-resident arrays (STORAGE | TRANSFER_SRC |
+ * TRANSFER_DST, no READBACK: read them back with zg_buffer_read_async or copy
+ * them).  Ops whose output array comes from a GpuOnly pool (add, relu, sgemm,
+ * gemm_bias_relu; in-place relu / saxpy / sscal on a GpuOnly array) are queued
+ * on the device stream and return without the per-dispatch synchronize;
+ * everything the host can do with those arrays is ordered after them on that
+ * stream.  Other values: ZG_ERR_UNSUPPORTED. */
+int zg_pool_create_with(zg_device *dev, uint32_t memory, zg_pool **out);
+/* The residency a pool's buffers are created with (ZG_MEMORY_*). */
+uint32_t zg_pool_memory(const zg_pool *pool);
 void zg_pool_destroy(zg_pool *pool);
 /* BufferPool::alloc (zengpu-compute/src/pool.rs:36-60). */
 int zg_pool_alloc(zg_pool *pool, const uint32_t *shape, uint32_t rank, uint32_t dtype,
@@ -361,9 +412,11 @@ int zg_sgemm_packed(int mode, int m, int n, int k, float alpha, const void *a_pa
  * fixed 64 MiB scratch array in the library's device image, held on every GPU
  * that loads it until the process exits.  Shapes whose scratch need
  * (zg_sgemm_workspace_bytes) exceeds 64 MiB are rejected with ZG_ERR_DISPATCH
- * (TF32X3 fits up to 2048^3).  Allocates nothing.  The first call on each
- * device looks up the array's device address (make it before any stream
- * capture).  All calls share the array: calls that overlap on the GPU race. */
+ * (TF32X3 fits up to 2048^3, BF16X3 up to 2880^3).  Allocates nothing.  The
+ * first call on each device looks up the array's device address (make it
+ * before any stream capture); a call under a new context of that device (after
+ * cudaDeviceReset) looks it up again.  All calls share the array: calls that
+ * overlap on the GPU race. */
 int zg_sgemm_f32_noalloc(int mode, int m, int n, int k, float alpha, const float *a,
                          const float *b, float *c, const float *bias, int relu, void *stream);
 

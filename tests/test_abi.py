@@ -137,3 +137,38 @@ def test_sgemm_kernel_name():
     assert name(0, 8192, 8192, 8192) == "sgemm_simt_kernel"
     assert name(3, 64, 64, 0) == "gemm_k0_kernel"
     assert name(9, 64, 64, 64) == "" and name(3, 0, 64, 64) == ""
+
+
+def test_release_workspaces_drops_cached_scratch():
+    """kernels.release_workspaces empties the per-(device, stream) GEMM scratch
+    cache, per device or all at once (no GPU needed: the cache is a dict)."""
+    import torch
+
+    from zengpu_b200 import kernels as K
+    saved = dict(K._workspaces)
+    try:
+        K._workspaces.clear()
+        K._workspaces.update({(0, 11): torch.empty(4), (0, 12): torch.empty(4),
+                              (1, 13): torch.empty(4)})
+        assert K.release_workspaces(0) == 2
+        assert list(K._workspaces) == [(1, 13)]
+        assert K.release_workspaces() == 1
+        assert not K._workspaces
+    finally:
+        K._workspaces.clear()
+        K._workspaces.update(saved)
+
+
+def test_last_error_detail_follows_the_last_status():
+    """zg_last_error_detail carries the status of the last failure on this
+    thread, with the structured fields empty for variants that have none."""
+    import ctypes as C
+
+    from zengpu_b200 import _lib as L
+    lib = L.load()
+    rc = lib.zg_sgemm_f32(99, 4, 4, 4, 1.0, None, None, None, None, 0, None, 0, None)
+    assert rc == 11  # Dispatch: unknown mode
+    d = L.last_error_detail()
+    assert d.status == 11 and d.handle_index == 0 and d.resource == b"" and d.needed == b""
+    assert lib.zg_pool_create_with(None, 0, C.byref(C.c_void_p())) == 12
+    assert L.last_error_detail().status == 12

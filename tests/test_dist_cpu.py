@@ -153,7 +153,8 @@ def test_panel_count():
 
 
 # ---- chained copy-engine broadcast: host-side protocol ------------------------------
-from zengpu_b200.dist import ChainedGemm, chain_neighbours, default_chunk_cols  # noqa: E402
+from zengpu_b200.dist import (  # noqa: E402
+    ChainBroken, ChainedGemm, ChainGuard, chain_neighbours, default_chunk_cols, pid_alive)
 
 
 @pytest.mark.parametrize("world,src", [(1, 0), (2, 0), (8, 0), (8, 3), (3, 2)])
@@ -188,6 +189,22 @@ class _FakeStream:
     def wait_stream(self, other):
         if self.log is not None:
             self.log.append(("wait_stream", other.name))
+
+
+class _FakeEvent:
+    """Completion marker of one step: steps recorded while `complete_new` is
+    set complete at once, the others only once an abort released them."""
+    complete_new = True
+    released = False
+
+    def __init__(self):
+        self.complete = _FakeEvent.complete_new
+
+    def record(self, stream):
+        pass
+
+    def query(self):
+        return self.complete or _FakeEvent.released
 
 
 class _FakeBuf:
@@ -246,6 +263,15 @@ class _FakeChainLib:
         self.log.append(("destroy",))
         return 0
 
+    def zg_bchain_abort(self, chain, epoch):
+        self.log.append(("abort", epoch))
+        _FakeEvent.released = True  # the aborted steps drain
+        return 0
+
+    def zg_kernel_status(self, code):
+        self.log.append(("status",))
+        return 0
+
 
 def _worker_chain(rank, world, port, src, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -257,6 +283,7 @@ def _worker_chain(rank, world, port, src, q):
         cg = ChainedGemm(k=64, n=512, mode=3, src=src, chunk_cols=256,
                          lib=_FakeChainLib(rank, log), ops=_FakeOps(log))
         cg.copy_stream = _FakeStream(log, "copy")
+        cg._new_event = _FakeEvent
         a = torch.zeros((10, 64))
         b = torch.zeros((64, 512)) if rank == src else None
         out = torch.zeros((10, 512))
@@ -325,3 +352,157 @@ def test_chained_gemm_rejects_mismatched_ranks():
     for p in procs:
         p.join(timeout=60)
     assert res == {0: True, 1: True}
+
+
+# ---- failure detection of the chain (host side, no GPU) -----------------------------
+class _Ev:
+    def __init__(self, done):
+        self.done = done
+
+    def query(self):
+        return self.done
+
+
+def test_chain_guard_deadline_and_pruning():
+    g = ChainGuard(0, [11, 22], None, 1, deadline_s=0.2, alive=lambda pid: True)
+    g.wait(5)  # never launched: nothing to wait for
+    g.launched(1, _Ev(True))
+    g.launched(2, _Ev(False))
+    g.launched(3, _Ev(True))
+    assert sorted(g.events) == [2, 3]  # only the last two steps are kept
+    assert g.in_flight()
+    g.wait(3)
+    import time as _t
+    t0 = _t.monotonic()
+    with pytest.raises(ChainBroken, match="step 2 did not complete within 0.2 s"):
+        g.wait(2)
+    assert _t.monotonic() - t0 < 2.0
+
+
+def test_chain_guard_neighbours():
+    alive = {11: True, 22: True, 33: True}
+    g = ChainGuard(1, [11, 22, 33], 0, 2, alive=lambda pid: alive[pid])
+    g.check_neighbours()
+    alive[33] = False
+    assert g.gone_neighbours() == [2]
+    with pytest.raises(ChainBroken, match="neighbour rank 2 \\(pid 33\\) has exited"):
+        g.check_neighbours()
+
+
+def test_pid_alive_sees_exit_and_zombies():
+    import subprocess
+    p = subprocess.Popen(["sleep", "30"])
+    try:
+        assert pid_alive(p.pid)
+        p.kill()
+        import time as _t
+        _t.sleep(0.2)  # killed, not yet reaped: a zombie counts as exited
+        assert not pid_alive(p.pid)
+    finally:
+        p.wait()
+    assert not pid_alive(p.pid)
+    assert pid_alive(os.getpid())
+
+
+def _worker_chain_leave(rank, world, port, mode, q):
+    """Two ranks run two steps; then rank 1 leaves (its process exits) or stops
+    taking part (stays alive, steps no more).  Rank 0's next step must raise
+    ChainBroken, and so must every step after it."""
+    import time as _t
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    log = []
+    torch.cuda.current_stream = lambda: _FakeStream(log, "compute")
+    cg = ChainedGemm(k=64, n=512, mode=3, src=0, chunk_cols=256, deadline_s=0.5,
+                     lib=_FakeChainLib(rank, log), ops=_FakeOps(log))
+    cg.copy_stream = _FakeStream(log, "copy")
+    cg._new_event = _FakeEvent
+    a = torch.zeros((10, 64))
+    b = torch.zeros((64, 512)) if rank == 0 else None
+    out = torch.zeros((10, 512))
+    for _ in range(2):
+        cg.step(a, b, out)
+    dist.barrier()
+    if rank == 1:
+        if mode == "stop":
+            q.get(timeout=60)  # stays alive, steps no more, until rank 0 is done
+        return
+    peer = cg.guard.pids[1]
+    if mode == "exit":
+        t0 = _t.monotonic()
+        while pid_alive(peer) and _t.monotonic() - t0 < 60:
+            _t.sleep(0.05)
+    else:
+        _FakeEvent.complete_new = False  # from here on, steps do not complete
+    results = []
+    for _ in range(4):
+        try:
+            cg.step(a, b, out)
+            results.append("ok")
+        except ChainBroken as e:
+            results.append(str(e))
+    cg.close()  # a broken chain is not freed (no collective, no hang)
+    if mode == "stop":
+        q.put("done")  # lets rank 1 exit
+    q.put((results, log))
+
+
+@pytest.mark.parametrize("mode", ["exit", "stop"])
+def test_chain_survivor_detects_a_peer_that_left(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_chain_leave, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    procs[0].join(timeout=120)
+    got = [q.get(timeout=10)]
+    while not isinstance(got[-1], tuple):
+        got.append(q.get(timeout=10))
+    results, log = got[-1]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    if mode == "exit":
+        # found before step 3 was queued: nothing launched, no abort needed
+        assert "neighbour rank 1" in results[0] and "has exited" in results[0]
+        assert ("source", 3) not in log and not any(e[0] == "abort" for e in log)
+    else:
+        # steps 3 and 4 are queued; step 5 waits for step 3, which never
+        # completes: the deadline expires, this rank's waits are opened
+        assert results[:2] == ["ok", "ok"]
+        assert "step 3 did not complete within 0.5 s" in results[2]
+        assert ("abort", 4) in log and ("status",) in log
+    assert results[-1] == results[-2]  # the chain stays broken
+    assert ("destroy",) not in log     # and keeps its memory
+
+
+def _worker_never_joins(rank, port, q):
+    import datetime
+    import time as _t
+    if rank == 1:
+        return  # this rank never joins the process group
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    t0 = _t.monotonic()
+    try:
+        dist.init_process_group("gloo", rank=0, world_size=2,
+                                timeout=datetime.timedelta(seconds=3))
+        q.put(("joined", _t.monotonic() - t0))
+    except Exception as e:  # noqa: BLE001 - the expected failure
+        q.put((type(e).__name__, _t.monotonic() - t0))
+
+
+def test_rank_that_never_joins_ends_the_others_with_an_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_never_joins, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    what, seconds = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert what != "joined"
+    assert seconds < 60

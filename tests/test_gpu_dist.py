@@ -107,3 +107,119 @@ def test_chained_gemm_source_not_rank0():
 @pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four GPUs")
 def test_chained_gemm_four_ranks():
     _run(4, mode=3, m_total=4096, n=4096, k=1024, chunk=256, src=2)
+
+
+def _worker_leave(rank, world, port, how, q, release):
+    """Two ranks run two chained steps; then one rank leaves between steps
+    (none of its work in flight): `exit` - its process ends; `stop` - it stays
+    alive but takes no further step.  The survivor must find out on the host
+    before it launches into the gone rank (pid check) or, for a rank that
+    stopped, when a step misses its deadline (then its own waits are opened
+    and its queued work drains), raise ChainBroken, and still compute a
+    correct one-GPU GEMM afterwards."""
+    import datetime
+    import time
+
+    import numpy as np
+    import torch.distributed as dist
+
+    import _oracle as O
+    from zengpu_b200 import kernels as K
+    from zengpu_b200.dist import ChainBroken, ChainedGemm, pid_alive, row_range
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    leaver = 1 if how in ("exit", "stop") else 0
+    result = {"rank": rank, "ok": False}
+    try:
+        m_total, n, k = 2048, 2048, 1024
+        r0, r1 = row_range(m_total, world, rank)
+        a = K.fill_uniform(torch.empty((r1 - r0, k), device="cuda"), 7 + rank)
+        cg = ChainedGemm(k, n, mode=4, src=0, chunk_cols=256, deadline_s=3.0)
+        out = torch.empty((r1 - r0, n), device="cuda")
+        b = K.fill_uniform(torch.empty((k, n), device="cuda"), 100)
+        for _ in range(2):
+            cg.step(a, b if rank == 0 else None, out)
+        torch.cuda.synchronize()
+        dist.barrier()  # every rank's two steps are complete
+        if rank == leaver:
+            result["ok"] = True
+            if how == "stop":
+                q.put(result)
+                release.get(timeout=120)  # stays alive until the survivor is done
+                return
+            return  # exit: the process ends here
+        peer = cg.guard.pids[leaver]
+        if how in ("exit", "exit0"):
+            t0 = time.monotonic()
+            while pid_alive(peer) and time.monotonic() - t0 < 60:
+                time.sleep(0.05)
+        outcomes = []
+        t0 = time.monotonic()
+        for _ in range(6):
+            try:
+                cg.step(a, b if rank == 0 else None, out)
+                outcomes.append("ok")
+            except ChainBroken as e:
+                outcomes.append(str(e))
+        elapsed = time.monotonic() - t0
+        torch.cuda.synchronize()
+        broken = [o for o in outcomes if o != "ok"]
+        # a fresh one-GPU GEMM on the survivor, on the same stream, is correct
+        x = O.uniform(300 * 200, 31).reshape(300, 200)
+        y = O.uniform(200 * 260, 32).reshape(200, 260)
+        c = K.sgemm(torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda(), mode=4)
+        torch.cuda.synchronize()
+        err = O.rel_fro(c.cpu().numpy(), O.sgemm(x, y))
+        result.update(outcomes=outcomes, elapsed=elapsed, err=err, status=K.kernel_status(),
+                      ok=bool(broken) and err <= 1e-5 and np.isfinite(err))
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        result["error"] = f"{type(e).__name__}: {e}"
+    finally:
+        gone = rank == leaver and how in ("exit", "exit0")
+        if not gone and not (rank == leaver and how == "stop"):
+            q.put(result)
+        if how == "stop" and rank != leaver:
+            release.put("done")  # lets the rank that stopped exit
+        if not gone:
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("how", ["exit", "exit0", "stop"])
+def test_chain_survivor_after_a_rank_leaves(how):
+    """exit: the last rank leaves; exit0: the source leaves; stop: the last
+    rank stays alive but stops stepping (the source's deadline expires)."""
+    ctx = mp.get_context("spawn")
+    q, release = ctx.Queue(), ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_leave, args=(r, 2, port, how, q, release), daemon=True)
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    survivor = 0 if how in ("exit", "stop") else 1
+    results = {}
+    deadline = 300
+    while survivor not in results:
+        item = q.get(timeout=deadline)
+        results[item["rank"]] = item
+    for p in procs:
+        p.join(timeout=120)
+    r = results[survivor]
+    assert r["ok"], r
+    if how == "stop":
+        # steps 3 to 6 are queued (3 and 4 complete: the stopped rank had
+        # released steps 1 and 2); the fifth call waits for step 5, whose copy
+        # to the stopped rank waits for it to release step 3: the deadline
+        # expires
+        assert r["outcomes"][:4] == ["ok"] * 4, r
+        assert "did not complete within 3 s" in r["outcomes"][4], r
+    else:
+        assert "has exited" in r["outcomes"][0], r
+        assert r["elapsed"] < 10, r
+    assert r["status"] == 0, r
+    for p in procs:
+        assert p.exitcode == 0

@@ -170,6 +170,28 @@ def test_default_mode_is_tf32x3(device):
 
 
 @pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
+def test_blas_sgemm_facade(device, pool, kats, mode):
+    """Blas::sgemm (zengpu-blas/src/lib.rs:74-83) delegates to its GemmKernel:
+    the 17 x 33 x 9 KAT exactly, a 300 x 260 x 190 product with alpha = -1.5
+    against the oracle, and the reference's shape errors."""
+    blas = zg.Blas(device)
+    assert blas.gemm.mode == zg.GemmMode.TF32X3  # the library default
+    blas.gemm.mode = mode
+    a = zg.upload(device, pool, kats["gemm_17x33x9_a"])
+    b = zg.upload(device, pool, kats["gemm_17x33x9_b"])
+    c = blas.sgemm(device, pool, 1.0, a, b)
+    np.testing.assert_array_equal(bits(zg.download(device, c)), bits(kats["gemm_17x33x9_c"]))
+    x = O.uniform(300 * 190, 81).reshape(300, 190)
+    y = O.uniform(190 * 260, 82).reshape(190, 260)
+    z = blas.sgemm(device, pool, -1.5, zg.upload(device, pool, x), zg.upload(device, pool, y))
+    assert z.shape == [300, 260]
+    assert O.rel_fro(zg.download(device, z), O.sgemm_ref(x, y, -1.5)) <= TOL[mode]
+    with pytest.raises(zg.Dispatch, match="inner dimensions mismatch"):
+        blas.sgemm(device, pool, 1.0, a, a)
+    blas.destroy(device)
+
+
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
 def test_packed_operands_into_column_panels(mode):
     """pack_a once, pack_b per column panel, each GEMM written into its column
     panel of a row-major C (pitch n) - the multi-GPU pipelined path."""
@@ -248,31 +270,6 @@ def test_8192_sampled_vs_fp64(mode):
     for r0, c0 in [(0, 0), (n - 256, n - 256), (3000, 5000)]:
         ref = O.dgemm_tile(a, b, r0, c0, 256, 256)
         assert O.rel_fro(c[r0:r0 + 256, c0:c0 + 256].cpu().numpy(), ref) <= TOL[mode]
-    del ta, tb, c
-    torch.cuda.empty_cache()
-
-
-def test_sharded_config_tiles_vs_fp64():
-    """32768 x 32768 x 8192 (seed 4) in 3xTF32, computed as two row shards the
-    way the multi-GPU path splits it; 16 random 128 x 128 tiles vs f64."""
-    m = n = 32768
-    k = 8192
-    ta = torch.empty((m, k), device="cuda")
-    tb = torch.empty((k, n), device="cuda")
-    K.fill_uniform(ta, 4)
-    K.fill_uniform(tb, 1004)
-    c = torch.empty((m, n), device="cuda")
-    for r0, r1 in [(0, m // 2), (m // 2, m)]:
-        K.sgemm(ta[r0:r1], tb, mode=zg.GemmMode.TF32X3, out=c[r0:r1])
-    torch.cuda.synchronize()
-    assert K.kernel_status() == 0
-    a, b = ta.cpu().numpy(), tb.cpu().numpy()
-    rng = np.random.default_rng(4)
-    for _ in range(16):
-        r0 = int(rng.integers(0, m // 128)) * 128
-        c0 = int(rng.integers(0, n // 128)) * 128
-        ref = O.dgemm_tile(a, b, r0, c0, 128, 128)
-        assert O.rel_fro(c[r0:r0 + 128, c0:c0 + 128].cpu().numpy(), ref) <= 1e-5
     del ta, tb, c
     torch.cuda.empty_cache()
 

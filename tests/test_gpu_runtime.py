@@ -5,7 +5,9 @@ from __future__ import annotations
 
 import numpy as np
 import pytest
+import torch
 
+import _oracle as O
 import zengpu_b200 as zg
 
 pytestmark = pytest.mark.gpu
@@ -61,11 +63,15 @@ def test_buffer_roundtrip_and_errors(device):
     with pytest.raises(zg.BindingMismatch, match="exceeds"):
         device.read_buffer(h, 60, 8)
     nr = device.create_buffer(16, U.STORAGE)
-    with pytest.raises(zg.MissingUsage):
+    with pytest.raises(zg.MissingUsage) as mu:
         device.read_buffer(nr, 0, 4)
+    # UsageError::MissingUsage's fields as zengpu-cuda/src/lib.rs:539-542 sets them
+    assert (mu.value.resource, mu.value.needed) == ("buffer", "READBACK")
     device.destroy_buffer(h)
-    with pytest.raises(zg.StaleHandle):
+    with pytest.raises(zg.StaleHandle) as st:
         device.write_buffer(h, 0, b"\0" * 4)
+    assert st.value.index == h.index and st.value.expected_gen == h.generation
+    assert st.value.actual_gen != h.generation
     device.destroy_buffer(h)  # stale destroy is a no-op
     device.destroy_buffer(nr)
 
@@ -190,3 +196,39 @@ def test_device_queries(device):
     assert device.device_ordinal() == 0
     assert device.can_peer(0)
     assert device.stream() != 0
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_copy_from_peer_two_devices(device):
+    """GpuDevice::can_peer / copy_from_peer (zengpu-hal/src/device.rs:91-106):
+    32 MiB + 12 bytes copied device 1 -> device 0 and back over NVLink, bit for
+    bit, at NVLink speed (direct peer copy once can_peer enabled access); a
+    copy longer than either buffer is rejected as the HIP backend does."""
+    other = zg.CudaDevice(1)
+    try:
+        assert device.can_peer(1) and other.can_peer(0)
+        n = (32 << 20) // 4 + 3
+        data = O.uniform(n, 91)
+        src = other.create_buffer(n * 4)
+        other.write_buffer(src, 0, data)
+        dst = device.create_buffer(n * 4)
+        device.copy_from_peer(dst, other, src, n * 4)
+        got = np.frombuffer(device.read_buffer(dst, 0, n * 4), np.float32)
+        np.testing.assert_array_equal(got.view(np.uint32), data.view(np.uint32))
+        back = other.create_buffer(n * 4)
+        other.copy_from_peer(back, device, dst, n * 4)
+        got2 = np.frombuffer(other.read_buffer(back, 0, n * 4), np.float32)
+        np.testing.assert_array_equal(got2.view(np.uint32), data.view(np.uint32))
+        import time
+        t0 = time.perf_counter()
+        for _ in range(5):
+            device.copy_from_peer(dst, other, src, n * 4)
+        gbs = 5 * n * 4 / (time.perf_counter() - t0) / 1e9
+        assert gbs > 100, gbs  # NVLink, not a copy staged through the host
+        with pytest.raises(zg.Backend, match="exceeds"):
+            device.copy_from_peer(dst, other, src, n * 4 + 4)
+        for h in (src, back):
+            other.destroy_buffer(h)
+        device.destroy_buffer(dst)
+    finally:
+        other.close()

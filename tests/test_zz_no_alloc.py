@@ -43,8 +43,11 @@ def _inputs(m, n, k, seed):
     return a, b, bias
 
 
-@pytest.mark.parametrize("mode", [zg.GemmMode.TF32X3, zg.GemmMode.TF32, zg.GemmMode.SIMT_FP32],
-                         ids=lambda m: m.name)
+MODES = [zg.GemmMode.BF16X3, zg.GemmMode.TF32_BF16X2, zg.GemmMode.TF32X3, zg.GemmMode.TF32,
+         zg.GemmMode.SIMT_FP32]
+
+
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
 def test_noalloc_matches_workspace_entry_point_twice(mode):
     torch.cuda.set_device(0)
     # two calls in a row with different shapes and data: the shared scratch
@@ -61,8 +64,37 @@ def test_noalloc_matches_workspace_entry_point_twice(mode):
         assert K.kernel_status() == 0
         if seed == 50:  # scratch already looked up and loaded: nothing may allocate now
             assert torch.cuda.mem_get_info()[0] == free_before
-        err = O.rel_fro(c.cpu().numpy(), c_ref.cpu().numpy())
+        got = c.cpu().numpy()
+        err = O.rel_fro(got, c_ref.cpu().numpy())
         assert err <= TOL[mode], err
+        # and against the oracle (the reference CPU backend's arithmetic)
+        an, bn = a.cpu().numpy(), b.cpu().numpy()
+        ref = (O.sgemm_bias_relu(an, bn, bias.cpu().numpy(), alpha=0.5) if relu
+               else O.sgemm(an, bn, 0.5))
+        err = O.rel_fro(got, ref)
+        assert err <= TOL[mode], err
+
+
+def test_noalloc_bf16x3_largest_cube_that_fits():
+    """BF16X3 needs 8 bytes of scratch per (m + n) * k: 2880^3 (63.3 MiB) is the
+    largest multiple of 64 that fits, and takes the CTA-pair kernel."""
+    torch.cuda.set_device(0)
+    s = 2880
+    mode = zg.GemmMode.BF16X3
+    assert K.workspace_bytes(mode, s, s, s) <= 64 << 20 < K.workspace_bytes(mode, s + 64, s + 64, s + 64)
+    for seed in (60, 61):
+        a = K.fill_uniform(torch.empty((s, s), device="cuda"), seed)
+        b = K.fill_uniform(torch.empty((s, s), device="cuda"), seed + 100)
+        c = torch.full((s, s), float("nan"), device="cuda")
+        assert _noalloc(a, b, c, mode) == 0, L.last_error()
+        ref = K.sgemm(a, b, mode=mode)
+        torch.cuda.synchronize()
+        assert K.kernel_status() == 0
+        assert torch.equal(c.view(torch.int32), ref.view(torch.int32))
+        an, bn = a.cpu().numpy(), b.cpu().numpy()
+        for r0, c0 in [(0, 0), (s - 128, s - 128)]:
+            tile = O.dgemm_tile(an, bn, r0, c0, 128, 128)
+            assert O.rel_fro(c[r0:r0 + 128, c0:c0 + 128].cpu().numpy(), tile) <= 1e-5
 
 
 def test_noalloc_rejects_shapes_beyond_the_static_scratch():

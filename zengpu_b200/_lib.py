@@ -28,6 +28,20 @@ class Handle(C.Structure):
         return hash((self.index, self.generation))
 
 
+class ErrorDetail(C.Structure):
+    _fields_ = [
+        ("status", C.c_int32),
+        ("handle_index", C.c_uint32),
+        ("expected_gen", C.c_uint32),
+        ("actual_gen", C.c_uint32),
+        ("memory", C.c_uint32),
+        ("reserved", C.c_uint32),
+        ("features", C.c_uint64),
+        ("resource", C.c_char_p),
+        ("needed", C.c_char_p),
+    ]
+
+
 class Scalar(C.Structure):
     _fields_ = [("kind", C.c_uint32), ("bits", C.c_uint32)]
 
@@ -82,6 +96,7 @@ _fp = C.c_void_p  # device float pointers travel as integers
 # name -> (restype, argtypes); mirrors include/zengpu_b200.h one to one.
 SIGNATURES: dict[str, tuple] = {
     "zg_last_error": (C.c_char_p, []),
+    "zg_last_error_detail": (_i, [C.POINTER(ErrorDetail)]),
     "zg_abi_version": (_i, []),
     "zg_device_count": (_i, [C.POINTER(_i)]),
     "zg_device_open": (_i, [_i, C.POINTER(_vp)]),
@@ -92,6 +107,7 @@ SIGNATURES: dict[str, tuple] = {
     "zg_buffer_create": (_i, [_vp, _u64, _u32, _u32, C.POINTER(Handle)]),
     "zg_buffer_write": (_i, [_vp, Handle, _u64, _vp, _u64]),
     "zg_buffer_read": (_i, [_vp, Handle, _u64, _vp, _u64]),
+    "zg_buffer_read_async": (_i, [_vp, Handle, _u64, _vp, _u64, C.POINTER(_vp)]),
     "zg_buffer_copy": (_i, [_vp, Handle, _u64, Handle, _u64, _u64]),
     "zg_buffer_destroy": (None, [_vp, Handle]),
     "zg_buffer_info": (_i, [_vp, Handle, C.POINTER(_u64), C.POINTER(_u64)]),
@@ -108,6 +124,8 @@ SIGNATURES: dict[str, tuple] = {
     "zg_submission_destroy": (None, [_vp]),
     "zg_size_class": (_u64, [_u64]),
     "zg_pool_create": (_i, [_vp, C.POINTER(_vp)]),
+    "zg_pool_create_with": (_i, [_vp, _u32, C.POINTER(_vp)]),
+    "zg_pool_memory": (_u32, [_vp]),
     "zg_pool_destroy": (None, [_vp]),
     "zg_pool_alloc": (_i, [_vp, C.POINTER(_u32), _u32, _u32, C.POINTER(CDeviceArray)]),
     "zg_pool_free": (None, [_vp, C.POINTER(CDeviceArray)]),
@@ -187,3 +205,9 @@ def load() -> C.CDLL:
 def last_error() -> str:
     msg = load().zg_last_error()
     return msg.decode() if msg else ""
+
+
+def last_error_detail() -> ErrorDetail:
+    d = ErrorDetail()
+    load().zg_last_error_detail(C.byref(d))
+    return d

@@ -57,8 +57,26 @@ _ERRORS = {cls.code: cls for cls in (
 
 
 def check(rc: int) -> None:
-    if rc != 0:
-        raise _ERRORS.get(rc, GpuError)(L.last_error())
+    """Raises the GpuError subclass of a non-zero status, with the reference's
+    structured fields where the variant has them (zg_last_error_detail):
+    StaleHandle.index / expected_gen / actual_gen, MissingUsage.resource /
+    needed, OutOfMemory.memory, UnsupportedFeatures.features."""
+    if rc == 0:
+        return
+    err = _ERRORS.get(rc, GpuError)(L.last_error())
+    d = L.last_error_detail()
+    if d.status == rc:
+        if rc == StaleHandle.code:
+            err.index, err.expected_gen, err.actual_gen = (d.handle_index, d.expected_gen,
+                                                           d.actual_gen)
+        elif rc == MissingUsage.code:
+            err.resource = (d.resource or b"").decode()
+            err.needed = (d.needed or b"").decode()
+        elif rc == OutOfMemory.code:
+            err.memory = MemoryUsage(d.memory)
+        elif rc == UnsupportedFeatures.code:
+            err.features = int(d.features)
+    raise err
 
 
 # ---- enums ----------------------------------------------------------------------
@@ -229,6 +247,21 @@ class CudaDevice:
         check(self._lib.zg_buffer_read(self._p, buffer, int(offset), C.c_void_p(host_ptr),
                                        int(length)))
 
+    def read_buffer_async(self, buffer: Handle, offset: int, dst, length: int | None = None
+                          ) -> "Submission":
+        """Queues a device -> host copy into `dst` (a host address, a numpy array
+        or a pinned torch CPU tensor) after everything queued before it and
+        returns the submission; `dst` holds the bytes once it completes
+        (zg_buffer_read_async).  Needs READBACK or TRANSFER_SRC usage."""
+        ptr, keep = _host_ptr_bytes(dst)
+        nbytes = keep[1] if length is None else int(length)
+        sub = C.c_void_p()
+        check(self._lib.zg_buffer_read_async(self._p, buffer, int(offset), C.c_void_p(ptr),
+                                             nbytes, C.byref(sub)))
+        s = Submission(sub)
+        s._keep = keep  # the destination must outlive the copy
+        return s
+
     def write_buffer_ptr(self, buffer: Handle, offset: int, host_ptr: int, length: int) -> None:
         check(self._lib.zg_buffer_write(self._p, buffer, int(offset), C.c_void_p(host_ptr),
                                         int(length)))
@@ -350,14 +383,23 @@ def size_class(size: int) -> int:
 
 
 class BufferPool:
-    """Size-classed (pow2, min 256 B) free list over device buffers."""
+    """Size-classed (pow2, min 256 B) free list over device buffers.
 
-    def __init__(self, device: CudaDevice):
+    memory=MemoryUsage.Upload is the reference's pool (STORAGE | READBACK,
+    zengpu-compute/src/pool.rs:47-51).  MemoryUsage.GpuOnly gives device-resident
+    arrays without READBACK: ops writing them are queued without a per-op
+    synchronize, and they are read back with download_async (or copied)."""
+
+    def __init__(self, device: CudaDevice, memory: MemoryUsage = MemoryUsage.Upload):
         self._lib = L.load()
         self.device = device
         p = C.c_void_p()
-        check(self._lib.zg_pool_create(device.raw, C.byref(p)))
+        check(self._lib.zg_pool_create_with(device.raw, int(memory), C.byref(p)))
         self._p = p
+
+    @property
+    def memory(self) -> MemoryUsage:
+        return MemoryUsage(int(self._lib.zg_pool_memory(self._p)))
 
     @property
     def raw(self) -> C.c_void_p:
@@ -401,6 +443,16 @@ def download(device: CudaDevice, array: DeviceArray) -> np.ndarray:
     return out
 
 
+def download_async(device: CudaDevice, array: DeviceArray, out=None):
+    """Queues the readback of `array` into `out` (a float32 numpy array of its
+    shape, or a pinned torch CPU tensor; allocated when None) and returns
+    (out, submission): `out` holds the values once the submission completes.
+    Works for GpuOnly arrays."""
+    if out is None:
+        out = np.empty(array.shape, dtype=np.float32)
+    return out, device.read_buffer_async(array.buffer, 0, out, array.size_bytes())
+
+
 # ---- kernels -------------------------------------------------------------------------------
 class ElementwiseKernels:
     """add / relu pipelines (zengpu-compute/src/elementwise.rs:51-146)."""
@@ -435,6 +487,20 @@ class ElementwiseKernels:
 
     def relu_inplace(self, device: CudaDevice, a: DeviceArray) -> None:
         check(self._lib.zg_elementwise_relu_inplace(C.byref(self._k), device.raw, C.byref(a._c)))
+
+
+def _host_ptr_bytes(x) -> tuple[int, tuple]:
+    """(address, (keep-alive, size in bytes)) of a host destination buffer: an
+    int address (size unknown: 0), a C-contiguous numpy array, or a CPU tensor."""
+    if isinstance(x, int):
+        return x, (None, 0)
+    if hasattr(x, "data_ptr"):
+        if x.is_cuda or not x.is_contiguous():
+            raise ValueError("host destination must be a contiguous CPU tensor")
+        return int(x.data_ptr()), (x, x.numel() * x.element_size())
+    if not isinstance(x, np.ndarray) or not x.flags["C_CONTIGUOUS"] or not x.flags["WRITEABLE"]:
+        raise ValueError("host destination must be a writeable C-contiguous numpy array")
+    return x.ctypes.data, (x, x.nbytes)
 
 
 def _host_ptr(x) -> tuple[int, object]:

@@ -13,6 +13,10 @@
 //  * buffer writes / reads / copies are refused while a submission is in
 //    flight, and destroys are deferred until it completes;
 //  * shape and dtype errors are GpuError::Dispatch with the reference text.
+// Added: a BufferPool may hand out GpuOnly (device-resident, not host
+// readable) arrays; ops whose output is such an array are queued on the device
+// stream without the per-dispatch synchronize, and zg_buffer_read_async reads
+// results back through a pollable submission.
 // What changed: the CUDA backend now runs hand-written sm_100a kernels linked
 // into this library ("builtin" shaders) instead of ZSL/SPIR-V, and can still
 // load caller cubins / PTX through the driver API.
@@ -39,6 +43,7 @@ namespace zg {
 // ---- errors -------------------------------------------------------------------
 namespace {
 thread_local std::string g_last_error;
+thread_local zg_error_detail g_detail{};
 }
 
 int set_error(int code, const char* fmt, ...) {
@@ -48,7 +53,26 @@ int set_error(int code, const char* fmt, ...) {
     vsnprintf(buf, sizeof(buf), fmt, ap);
     va_end(ap);
     g_last_error = buf;
+    g_detail = zg_error_detail{};
+    g_detail.status = code;
+    g_detail.memory = ZG_MEMORY_GPU_ONLY;  // a CUDA allocation (zengpu-cuda/src/error.rs:18)
+    g_detail.resource = "";
+    g_detail.needed = "";
     return code;
+}
+
+// UsageError::MissingUsage with the reference's field values
+// (zengpu-cuda/src/lib.rs:539-542, 645-654).
+int missing_usage(const char* resource, const char* needed, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    set_error(ZG_ERR_MISSING_USAGE, "%s", buf);
+    g_detail.resource = resource;
+    g_detail.needed = needed;
+    return ZG_ERR_MISSING_USAGE;
 }
 
 // CUDA runtime error -> status, following zengpu-cuda/src/error.rs:16-36.
@@ -266,6 +290,9 @@ struct zg_device {
     // Submissions not yet observed complete, and frees deferred until then.
     std::vector<cudaEvent_t> pending;
     std::vector<uint32_t> deferred_buffers;  // retired slot indices
+    // A tensor-core GEMM was queued without a synchronize since the device
+    // status word was last read: the next readback submission checks it.
+    bool status_unchecked = false;
     void* workspace = nullptr;
     uint64_t workspace_bytes = 0;
     // Pipelined host-buffer GEMM: copy streams and device staging.
@@ -273,16 +300,22 @@ struct zg_device {
     cudaStream_t d2h = nullptr;
     void* staging = nullptr;
     uint64_t staging_bytes = 0;
+    // can_peer results: peer ordinal -> usable (peer access enabled)
+    std::unordered_map<int, bool> peer_access;
 };
 
 struct zg_submission {
     zg_device* dev = nullptr;
     cudaEvent_t event = nullptr;
     bool done = false;
+    // read the device status word once complete (bounded on-device waits of
+    // GEMMs queued without a synchronize before this submission)
+    bool check_status = false;
 };
 
 struct zg_pool {
     zg_device* dev = nullptr;
+    uint32_t memory = ZG_MEMORY_UPLOAD;  // residency of the buffers it creates
     std::mutex mu;
     std::unordered_map<uint64_t, std::vector<zg_handle>> free;
 };
@@ -319,8 +352,12 @@ void release_submission(zg_device* dev, cudaEvent_t ev) {
 bool in_flight(zg_device* dev) { return !dev->pending.empty(); }
 
 int stale(const char* what, zg_handle h, uint32_t actual) {
-    return set_error(ZG_ERR_STALE_HANDLE, "%s: stale handle (index %u, generation %u, current %u)",
-                     what, h.index, h.generation, actual);
+    set_error(ZG_ERR_STALE_HANDLE, "%s: stale handle (index %u, generation %u, current %u)",
+              what, h.index, h.generation, actual);
+    g_detail.handle_index = h.index;
+    g_detail.expected_gen = h.generation;
+    g_detail.actual_gen = actual;
+    return ZG_ERR_STALE_HANDLE;
 }
 
 int ensure_workspace(zg_device* dev, uint64_t bytes) {
@@ -459,7 +496,8 @@ int launch_op(zg_device* dev, const zg_dispatch_op* op, int mode_override) {
 int finish_sync(zg_device* dev, bool check_status) {
     int rc = cuda_status(cudaStreamSynchronize(dev->stream), "synchronize");
     if (rc) return rc;
-    if (check_status) {
+    if (check_status || dev->status_unchecked) {
+        dev->status_unchecked = false;
         uint32_t code = 0;
         if ((rc = zg_kernel_status(&code))) return rc;
         if (code)
@@ -470,15 +508,44 @@ int finish_sync(zg_device* dev, bool check_status) {
     return ZG_OK;
 }
 
+bool is_gemm_pipeline(zg_device* dev, zg_handle pipeline) {
+    Pipeline* p = dev->pipelines.get(pipeline);
+    return p && (p->builtin == kSgemmF32 || p->builtin == kSgemmBiasReluF32);
+}
+
 int dispatch_sync(zg_device* dev, const zg_dispatch_op* op, int mode_override) {
     int rc = launch_op(dev, op, mode_override);
     if (rc) {
         cudaStreamSynchronize(dev->stream);
         return rc;
     }
-    Pipeline* p = dev->pipelines.get(op->pipeline);
-    const bool tc = p && (p->builtin == kSgemmF32 || p->builtin == kSgemmBiasReluF32);
-    return finish_sync(dev, tc);
+    return finish_sync(dev, is_gemm_pipeline(dev, op->pipeline));
+}
+
+// Queues the op on the device stream and returns without waiting: for ops
+// whose output is a GpuOnly array, which the host can only observe through
+// stream-ordered calls (copy, readback submission, synchronous write / read
+// of other buffers), so the reference's per-dispatch wait buys nothing.  Host
+// errors and launch errors are still returned here; a bounded on-device wait
+// that expires is reported by the next readback submission.
+int dispatch_deferred(zg_device* dev, const zg_dispatch_op* op, int mode_override) {
+    std::lock_guard<std::recursive_mutex> lk(dev->mu);
+    int rc = set_device(dev);
+    if (rc) return rc;
+    if ((rc = launch_op(dev, op, mode_override))) {
+        cudaStreamSynchronize(dev->stream);
+        return rc;
+    }
+    if (is_gemm_pipeline(dev, op->pipeline)) dev->status_unchecked = true;
+    return ZG_OK;
+}
+
+// The residency of a live buffer (ZG_MEMORY_UPLOAD when the handle is stale;
+// the op that uses it reports the stale handle).
+uint32_t buffer_memory(zg_device* dev, zg_handle h) {
+    std::lock_guard<std::recursive_mutex> lk(dev->mu);
+    Buffer* b = dev->buffers.get(h);
+    return b ? b->memory : ZG_MEMORY_UPLOAD;
 }
 
 }  // namespace
@@ -489,6 +556,13 @@ int dispatch_sync(zg_device* dev, const zg_dispatch_op* op, int mode_override) {
 // ======================================================================
 
 extern "C" const char* zg_last_error(void) { return g_last_error.c_str(); }
+extern "C" int zg_last_error_detail(zg_error_detail* out) {
+    if (!out) return ZG_ERR_BACKEND;
+    *out = g_detail;
+    if (!out->resource) out->resource = "";
+    if (!out->needed) out->needed = "";
+    return ZG_OK;
+}
 extern "C" int zg_abi_version(void) { return ZG_ABI_VERSION; }
 
 extern "C" int zg_device_count(int* count) {
@@ -550,18 +624,29 @@ extern "C" void zg_device_close(zg_device* dev) {
 extern "C" int zg_device_ordinal(const zg_device* dev) { return dev ? dev->ordinal : -1; }
 extern "C" void* zg_device_stream(zg_device* dev) { return dev ? dev->stream : nullptr; }
 
+// GpuDevice::can_peer as the HIP backend implements it (zengpu-hip/src/lib.rs:
+// 613-631): true once this device can access the peer's memory, enabling that
+// access on first use; the answer is cached per peer.
+bool peer_usable(zg_device* dev, int peer_ordinal) {
+    std::lock_guard<std::recursive_mutex> lk(dev->mu);
+    if (peer_ordinal == dev->ordinal) return true;
+    auto it = dev->peer_access.find(peer_ordinal);
+    if (it != dev->peer_access.end()) return it->second;
+    int can = 0;
+    bool usable = cudaDeviceCanAccessPeer(&can, dev->ordinal, peer_ordinal) == cudaSuccess && can &&
+                  cudaSetDevice(dev->ordinal) == cudaSuccess;
+    if (usable) {
+        const cudaError_t e = cudaDeviceEnablePeerAccess(peer_ordinal, 0);
+        usable = e == cudaSuccess || e == cudaErrorPeerAccessAlreadyEnabled;
+    }
+    cudaGetLastError();  // a refused query or an already-enabled peer is not an error
+    dev->peer_access[peer_ordinal] = usable;
+    return usable;
+}
+
 extern "C" int zg_device_can_peer(zg_device* dev, int peer_ordinal, int* out) {
     if (!dev || !out) return set_error(ZG_ERR_BACKEND, "zg_device_can_peer: null argument");
-    int can = 0;
-    *out = 0;
-    if (peer_ordinal == dev->ordinal) {
-        *out = 1;
-        return ZG_OK;
-    }
-    int rc = cuda_status(cudaDeviceCanAccessPeer(&can, dev->ordinal, peer_ordinal),
-                         "cudaDeviceCanAccessPeer");
-    if (rc) return rc;
-    *out = can ? 1 : 0;
+    *out = peer_usable(dev, peer_ordinal) ? 1 : 0;
     return ZG_OK;
 }
 
@@ -579,9 +664,12 @@ extern "C" int zg_buffer_create(zg_device* dev, uint64_t size, uint32_t usage, u
         cudaError_t e = cudaMalloc(&b.ptr, size);
         if (e != cudaSuccess) {
             cudaGetLastError();
-            if (e == cudaErrorMemoryAllocation)
-                return set_error(ZG_ERR_OUT_OF_MEMORY, "out of memory allocating %llu bytes",
-                                 (unsigned long long)size);
+            if (e == cudaErrorMemoryAllocation) {
+                set_error(ZG_ERR_OUT_OF_MEMORY, "out of memory allocating %llu bytes",
+                          (unsigned long long)size);
+                g_detail.memory = memory;
+                return ZG_ERR_OUT_OF_MEMORY;
+            }
             return cuda_status(e, "cudaMalloc");
         }
     }
@@ -629,7 +717,7 @@ extern "C" int zg_buffer_read(zg_device* dev, zg_handle h, uint64_t offset, void
     Buffer* b = dev->buffers.get(h);
     if (!b) return stale("read_buffer", h, dev->buffers.current_gen(h.index));
     if (!(b->usage & ZG_USAGE_READBACK))
-        return set_error(ZG_ERR_MISSING_USAGE, "buffer needs READBACK usage");
+        return missing_usage("buffer", "READBACK", "buffer needs READBACK usage");
     if (in_flight(dev))
         return set_error(ZG_ERR_BINDING_MISMATCH,
                          "read_buffer_into cannot observe buffers while an asynchronous "
@@ -649,6 +737,44 @@ extern "C" int zg_buffer_read(zg_device* dev, zg_handle h, uint64_t offset, void
     return cuda_status(cudaStreamSynchronize(dev->stream), "read_buffer sync");
 }
 
+extern "C" int zg_buffer_read_async(zg_device* dev, zg_handle h, uint64_t offset, void* dst,
+                                    uint64_t len, zg_submission** out) {
+    if (!dev || !out) return set_error(ZG_ERR_BACKEND, "zg_buffer_read_async: null argument");
+    *out = nullptr;
+    std::lock_guard<std::recursive_mutex> lk(dev->mu);
+    Buffer* b = dev->buffers.get(h);
+    if (!b) return stale("read_buffer_async", h, dev->buffers.current_gen(h.index));
+    if (!(b->usage & (ZG_USAGE_READBACK | ZG_USAGE_TRANSFER_SRC)))
+        return missing_usage("buffer", "READBACK", "buffer needs READBACK or TRANSFER_SRC usage");
+    if (offset > b->len || len > b->len - offset)
+        return set_error(ZG_ERR_BINDING_MISMATCH, "cuda: read range %llu..%llu exceeds %llu",
+                         (unsigned long long)offset, (unsigned long long)(offset + len),
+                         (unsigned long long)b->len);
+    if (len && !dst) return set_error(ZG_ERR_BACKEND, "read_buffer_async: null destination");
+    int rc = set_device(dev);
+    if (rc) return rc;
+    if (len)
+        rc = cuda_status(cudaMemcpyAsync(dst, static_cast<uint8_t*>(b->ptr) + offset, len,
+                                         cudaMemcpyDeviceToHost, dev->stream),
+                         "read_buffer_async");
+    if (rc) return rc;
+    cudaEvent_t ev;
+    if ((rc = cuda_status(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "event create")))
+        return rc;
+    if ((rc = cuda_status(cudaEventRecord(ev, dev->stream), "event record"))) {
+        cudaEventDestroy(ev);
+        return rc;
+    }
+    dev->pending.push_back(ev);
+    auto* sub = new zg_submission();
+    sub->dev = dev;
+    sub->event = ev;
+    sub->check_status = dev->status_unchecked;
+    dev->status_unchecked = false;
+    *out = sub;
+    return ZG_OK;
+}
+
 extern "C" int zg_buffer_copy(zg_device* dev, zg_handle src, uint64_t src_offset, zg_handle dst,
                               uint64_t dst_offset, uint64_t len) {
     if (!dev) return set_error(ZG_ERR_BACKEND, "zg_buffer_copy: null device");
@@ -661,9 +787,11 @@ extern "C" int zg_buffer_copy(zg_device* dev, zg_handle src, uint64_t src_offset
     Buffer* d = dev->buffers.get(dst);
     if (!d) return set_error(ZG_ERR_BACKEND, "cuda: invalid destination buffer handle");
     if (!(s->usage & ZG_USAGE_TRANSFER_SRC))
-        return set_error(ZG_ERR_MISSING_USAGE, "source buffer needs TRANSFER_SRC usage");
+        return missing_usage("source buffer", "TRANSFER_SRC",
+                             "source buffer needs TRANSFER_SRC usage");
     if (!(d->usage & ZG_USAGE_TRANSFER_DST))
-        return set_error(ZG_ERR_MISSING_USAGE, "destination buffer needs TRANSFER_DST usage");
+        return missing_usage("destination buffer", "TRANSFER_DST",
+                             "destination buffer needs TRANSFER_DST usage");
     if (src.index == dst.index)
         return set_error(ZG_ERR_BINDING_MISMATCH,
                          "copy_buffer requires distinct source and destination buffers");
@@ -697,42 +825,71 @@ extern "C" void zg_buffer_destroy(zg_device* dev, zg_handle h) {
     }
     if (dev->buffers.remove(h, &b) && b.ptr) {
         cudaSetDevice(dev->ordinal);
+        // ops queued without a synchronize (GpuOnly outputs) may still read it
+        cudaStreamSynchronize(dev->stream);
         cudaFree(b.ptr);
     }
 }
 
+// GpuDevice::copy_from_peer (zengpu-hal/src/device.rs:96-106), as the HIP
+// backend does it (zengpu-hip/src/lib.rs:633-710): a direct peer copy over
+// NVLink when can_peer holds, else staged through host memory; synchronous.
 extern "C" int zg_buffer_copy_from_peer(zg_device* dst_dev, zg_handle dst, zg_device* src_dev,
                                         zg_handle src, uint64_t bytes) {
     if (!dst_dev || !src_dev) return set_error(ZG_ERR_BACKEND, "copy_from_peer: null device");
     void *dptr = nullptr, *sptr = nullptr;
     uint64_t dlen = 0, slen = 0;
     {
+        std::lock_guard<std::recursive_mutex> lk(dst_dev->mu);
+        Buffer* d = dst_dev->buffers.get(dst);
+        if (!d) return stale("copy_from_peer destination", dst, dst_dev->buffers.current_gen(dst.index));
+        if (in_flight(dst_dev))
+            return set_error(ZG_ERR_BINDING_MISMATCH,
+                             "copy_from_peer cannot run while a submission is pending");
+        dptr = d->ptr;
+        dlen = d->len;
+    }
+    {
         std::lock_guard<std::recursive_mutex> lk(src_dev->mu);
         Buffer* s = src_dev->buffers.get(src);
-        if (!s) return set_error(ZG_ERR_BACKEND, "cuda: invalid source buffer handle");
+        if (!s) return stale("copy_from_peer source", src, src_dev->buffers.current_gen(src.index));
         if (in_flight(src_dev))
             return set_error(ZG_ERR_BINDING_MISMATCH,
                              "copy_from_peer cannot run while the source device has pending work");
         sptr = s->ptr;
         slen = s->len;
+        // work queued on the source device without a synchronize (GpuOnly
+        // outputs) completes before its buffer is read
+        cudaSetDevice(src_dev->ordinal);
+        int rc = cuda_status(cudaStreamSynchronize(src_dev->stream), "copy_from_peer source sync");
+        if (rc) return rc;
     }
-    std::lock_guard<std::recursive_mutex> lk(dst_dev->mu);
-    Buffer* d = dst_dev->buffers.get(dst);
-    if (!d) return set_error(ZG_ERR_BACKEND, "cuda: invalid destination buffer handle");
-    if (in_flight(dst_dev))
-        return set_error(ZG_ERR_BINDING_MISMATCH,
-                         "copy_from_peer cannot run while a submission is pending");
-    dptr = d->ptr;
-    dlen = d->len;
     if (bytes > slen || bytes > dlen)
-        return set_error(ZG_ERR_BINDING_MISMATCH, "copy_from_peer: %llu bytes exceed a buffer",
-                         (unsigned long long)bytes);
+        return set_error(ZG_ERR_BACKEND,
+                         "cuda: peer copy of %llu bytes exceeds source (%llu) or destination (%llu) "
+                         "buffer",
+                         (unsigned long long)bytes, (unsigned long long)slen,
+                         (unsigned long long)dlen);
     if (bytes == 0) return ZG_OK;
-    int rc = set_device(dst_dev);
-    if (rc) return rc;
-    rc = cuda_status(cudaMemcpyPeerAsync(dptr, dst_dev->ordinal, sptr, src_dev->ordinal, bytes,
-                                         dst_dev->stream),
-                     "cudaMemcpyPeerAsync");
+    std::lock_guard<std::recursive_mutex> lk(dst_dev->mu);
+    int rc;
+    if (peer_usable(dst_dev, src_dev->ordinal)) {
+        if ((rc = set_device(dst_dev))) return rc;
+        rc = cuda_status(cudaMemcpyPeerAsync(dptr, dst_dev->ordinal, sptr, src_dev->ordinal, bytes,
+                                             dst_dev->stream),
+                         "cudaMemcpyPeerAsync");
+        if (rc) return rc;
+        return cuda_status(cudaStreamSynchronize(dst_dev->stream), "copy_from_peer sync");
+    }
+    std::vector<uint8_t> staging(bytes);
+    if ((rc = cuda_status(cudaSetDevice(src_dev->ordinal), "cudaSetDevice peer source")) ||
+        (rc = cuda_status(cudaMemcpy(staging.data(), sptr, bytes, cudaMemcpyDeviceToHost),
+                          "peer copy staging D2H")))
+        return rc;
+    if ((rc = set_device(dst_dev))) return rc;
+    rc = cuda_status(cudaMemcpyAsync(dptr, staging.data(), bytes, cudaMemcpyHostToDevice,
+                                     dst_dev->stream),
+                     "peer copy staging H2D");
     if (rc) return rc;
     return cuda_status(cudaStreamSynchronize(dst_dev->stream), "copy_from_peer sync");
 }
@@ -882,12 +1039,17 @@ extern "C" int zg_submit_batch(zg_device* dev, const zg_dispatch_op* ops, uint32
     auto* sub = new zg_submission();
     sub->dev = dev;
     sub->event = ev;
+    sub->check_status = dev->status_unchecked;
+    for (uint32_t i = 0; i < count; ++i)
+        if (is_gemm_pipeline(dev, ops[i].pipeline)) sub->check_status = true;
+    dev->status_unchecked = false;
     *out = sub;
     return ZG_OK;
 }
 
 extern "C" int zg_submission_poll(zg_submission* sub, int* done) {
     if (!sub || !done) return set_error(ZG_ERR_BACKEND, "zg_submission_poll: null argument");
+    int status_rc = ZG_OK;
     if (!sub->done) {
         std::lock_guard<std::recursive_mutex> lk(sub->dev->mu);
         cudaSetDevice(sub->dev->ordinal);
@@ -896,6 +1058,17 @@ extern "C" int zg_submission_poll(zg_submission* sub, int* done) {
             sub->done = true;
             release_submission(sub->dev, sub->event);
             sub->event = nullptr;
+            if (sub->check_status) {
+                // GEMMs queued before this submission without a synchronize
+                sub->check_status = false;
+                uint32_t code = 0;
+                status_rc = zg_kernel_status(&code);
+                if (!status_rc && code)
+                    status_rc = set_error(ZG_ERR_KERNEL_WAIT,
+                                          "kernel bounded wait expired (status 0x%x); results of "
+                                          "the work before this submission are invalid",
+                                          code);
+            }
         } else if (e == cudaErrorNotReady) {
             cudaGetLastError();
         } else {
@@ -903,7 +1076,7 @@ extern "C" int zg_submission_poll(zg_submission* sub, int* done) {
         }
     }
     *done = sub->done ? 1 : 0;
-    return ZG_OK;
+    return status_rc;
 }
 
 extern "C" int zg_submission_wait(zg_submission* sub, uint64_t timeout_ns) {
@@ -1040,11 +1213,23 @@ extern "C" uint64_t zg_size_class(uint64_t size) {
 }
 
 extern "C" int zg_pool_create(zg_device* dev, zg_pool** out) {
+    return zg_pool_create_with(dev, ZG_MEMORY_UPLOAD, out);
+}
+
+extern "C" int zg_pool_create_with(zg_device* dev, uint32_t memory, zg_pool** out) {
     if (!dev || !out) return set_error(ZG_ERR_BACKEND, "zg_pool_create: null argument");
+    if (memory != ZG_MEMORY_UPLOAD && memory != ZG_MEMORY_GPU_ONLY)
+        return set_error(ZG_ERR_UNSUPPORTED, "BufferPool: memory usage %u (Upload or GpuOnly)",
+                         memory);
     auto* p = new zg_pool();
     p->dev = dev;
+    p->memory = memory;
     *out = p;
     return ZG_OK;
+}
+
+extern "C" uint32_t zg_pool_memory(const zg_pool* pool) {
+    return pool ? pool->memory : ZG_MEMORY_UPLOAD;
 }
 
 extern "C" void zg_pool_destroy(zg_pool* pool) {
@@ -1093,8 +1278,13 @@ extern "C" int zg_pool_alloc(zg_pool* pool, const uint32_t* shape, uint32_t rank
         }
     }
     if (!have) {
-        int rc = zg_buffer_create(pool->dev, cls, ZG_USAGE_STORAGE | ZG_USAGE_READBACK,
-                                  ZG_MEMORY_UPLOAD, &h);
+        // Upload (the reference's pool): host-readable STORAGE | READBACK.
+        // GpuOnly: device resident, read back only through a copy or a
+        // readback submission.
+        const uint32_t usage = pool->memory == ZG_MEMORY_GPU_ONLY
+                                   ? ZG_USAGE_STORAGE | ZG_USAGE_TRANSFER_SRC | ZG_USAGE_TRANSFER_DST
+                                   : ZG_USAGE_STORAGE | ZG_USAGE_READBACK;
+        int rc = zg_buffer_create(pool->dev, cls, usage, pool->memory, &h);
         if (rc) return rc;
     }
     a.buffer = h;
@@ -1153,7 +1343,8 @@ extern "C" int zg_elementwise_add(const zg_elementwise_kernels* k, zg_device* de
     const uint32_t bufs[3] = {a->buffer.index, b->buffer.index, out->buffer.index};
     const zg_scalar sc[1] = {u32s(n)};
     zg_dispatch_op op = make_op(k->add_pipeline, bufs, 3, sc, 1, (n + 255) / 256, 1);
-    return zg_dispatch(dev, &op);
+    return pool->memory == ZG_MEMORY_GPU_ONLY ? dispatch_deferred(dev, &op, -1)
+                                              : zg_dispatch(dev, &op);
 }
 
 extern "C" int zg_elementwise_relu(const zg_elementwise_kernels* k, zg_device* dev, zg_pool* pool,
@@ -1168,7 +1359,8 @@ extern "C" int zg_elementwise_relu(const zg_elementwise_kernels* k, zg_device* d
     const uint32_t bufs[2] = {a->buffer.index, out->buffer.index};
     const zg_scalar sc[1] = {u32s(n)};
     zg_dispatch_op op = make_op(k->relu_pipeline, bufs, 2, sc, 1, (n + 255) / 256, 1);
-    return zg_dispatch(dev, &op);
+    return pool->memory == ZG_MEMORY_GPU_ONLY ? dispatch_deferred(dev, &op, -1)
+                                              : zg_dispatch(dev, &op);
 }
 
 extern "C" int zg_elementwise_relu_inplace(const zg_elementwise_kernels* k, zg_device* dev,
@@ -1182,7 +1374,8 @@ extern "C" int zg_elementwise_relu_inplace(const zg_elementwise_kernels* k, zg_d
     const uint32_t bufs[2] = {a->buffer.index, a->buffer.index};
     const zg_scalar sc[1] = {u32s(n)};
     zg_dispatch_op op = make_op(k->relu_pipeline, bufs, 2, sc, 1, (n + 255) / 256, 1);
-    return zg_dispatch(dev, &op);
+    return buffer_memory(dev, a->buffer) == ZG_MEMORY_GPU_ONLY ? dispatch_deferred(dev, &op, -1)
+                                                               : zg_dispatch(dev, &op);
 }
 
 extern "C" int zg_gemm_new(zg_device* dev, zg_gemm_kernel* out) {
@@ -1247,15 +1440,17 @@ int gemm_dispatch(const zg_gemm_kernel* kern, zg_device* dev, zg_pool* pool, flo
     const zg_scalar sc[4] = {u32s(m), u32s(n), u32s(k), f32s(alpha)};
     std::lock_guard<std::recursive_mutex> lk(dev->mu);
     if ((rc = set_device(dev))) return rc;
+    const bool deferred = pool->memory == ZG_MEMORY_GPU_ONLY;
     if (bias) {
         const uint32_t bufs[4] = {a->buffer.index, b->buffer.index, bias->buffer.index,
                                   out->buffer.index};
         zg_dispatch_op op = make_op(kern->fused_pipeline, bufs, 4, sc, 4, (n + 15) / 16, (m + 15) / 16);
-        return dispatch_sync(dev, &op, kern->mode);
+        return deferred ? dispatch_deferred(dev, &op, kern->mode)
+                        : dispatch_sync(dev, &op, kern->mode);
     }
     const uint32_t bufs[3] = {a->buffer.index, b->buffer.index, out->buffer.index};
     zg_dispatch_op op = make_op(kern->pipeline, bufs, 3, sc, 4, (n + 15) / 16, (m + 15) / 16);
-    return dispatch_sync(dev, &op, kern->mode);
+    return deferred ? dispatch_deferred(dev, &op, kern->mode) : dispatch_sync(dev, &op, kern->mode);
 }
 }  // namespace
 }  // namespace zg
@@ -1309,6 +1504,7 @@ extern "C" int zg_level1_saxpy(zg_device* dev, float alpha, const zg_device_arra
     if ((rc = level1_ptr(dev, x, &px)) || (rc = level1_ptr(dev, y, &py))) return rc;
     if ((rc = set_device(dev))) return rc;
     if ((rc = zg_saxpy_f32(alpha, px, py, n, dev->stream))) return rc;
+    if (buffer_memory(dev, y->buffer) == ZG_MEMORY_GPU_ONLY) return ZG_OK;  // queued, see dispatch_deferred
     return finish_sync(dev, false);
 }
 
@@ -1325,6 +1521,7 @@ extern "C" int zg_level1_sscal(zg_device* dev, float alpha, const zg_device_arra
     if ((rc = level1_ptr(dev, x, &px))) return rc;
     if ((rc = set_device(dev))) return rc;
     if ((rc = zg_sscal_f32(alpha, px, n, dev->stream))) return rc;
+    if (buffer_memory(dev, x->buffer) == ZG_MEMORY_GPU_ONLY) return ZG_OK;  // queued, see dispatch_deferred
     return finish_sync(dev, false);
 }
 

@@ -19,12 +19,15 @@
 // Host code must not pass the array's name to a kernel: on the host it is
 // only a stand-in symbol, not a device address.  The first call on each
 // device (with that device current) looks up the real device address with
-// cudaGetSymbolAddress and caches it; make that first call before any stream
-// capture.  All calls share the one array and it keeps the last call's
-// contents; nothing in it needs to start at zero (the pre-pass writes every
-// element the GEMM kernel then reads).  Calls whose work overlaps on the GPU
-// (different streams, or several host threads) race on the array: serialise
-// them, e.g. on one stream.
+// cudaGetSymbolAddress and caches it together with the CUDA context it belongs
+// to; a later call under a different context (the primary context torn down by
+// cudaDeviceReset and created again, which reloads the module) looks it up
+// again.  Make the first call before any stream capture.  All calls share the
+// one array and it keeps the last call's contents; nothing in it needs to
+// start at zero (the pre-pass writes every element the GEMM kernel then
+// reads).  Calls whose work overlaps on the GPU (different streams, or several
+// host threads) race on the array: serialise them, e.g. on one stream.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -42,9 +45,33 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes]
 
 std::mutex g_scratch_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device; looked up once
-// per device with that device current.
+// The CUDA context current on this thread, or null when none is (cuCtxGetCurrent,
+// found through the runtime so the library keeps no link-time dependency on
+// libcuda).
+int current_context(CUcontext* ctx) {
+    using Fn = CUresult (*)(CUcontext*);
+    static Fn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault,
+                                             &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<Fn>(p);
+    });
+    *ctx = nullptr;
+    if (!fn) return set_error(ZG_ERR_BACKEND, "zg_sgemm_f32_noalloc: cuCtxGetCurrent unavailable");
+    if (fn(ctx) != CUDA_SUCCESS)
+        return set_error(ZG_ERR_BACKEND, "zg_sgemm_f32_noalloc: cuCtxGetCurrent failed");
+    return ZG_OK;
+}
+
+// Device address of the scratch array on the current device; looked up with
+// that device current, once per (device, context).  A thread with no context
+// current yet gets the runtime's primary context from the lookup itself.
 int scratch_for_current_device(void** out) {
     int dev = 0;
     int rc = cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
@@ -52,14 +79,18 @@ int scratch_for_current_device(void** out) {
     if (dev < 0 || dev >= kMaxDevices)
         return set_error(ZG_ERR_UNSUPPORTED, "zg_sgemm_f32_noalloc: device ordinal %d above %d",
                          dev, kMaxDevices - 1);
+    CUcontext ctx = nullptr;
+    if ((rc = current_context(&ctx))) return rc;
     std::lock_guard<std::mutex> lk(g_scratch_mu);
-    if (!g_scratch_ptr[dev]) {
+    if (!ctx || !g_scratch_ptr[dev] || g_scratch_ctx[dev] != ctx) {
         void* p = nullptr;
         rc = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch),
                          "cudaGetSymbolAddress(scratch)");
         if (rc) return rc;
         if (!p) return set_error(ZG_ERR_BACKEND, "zg_sgemm_f32_noalloc: null scratch address");
+        if ((rc = current_context(&ctx))) return rc;
         g_scratch_ptr[dev] = p;
+        g_scratch_ctx[dev] = ctx;
     }
     *out = g_scratch_ptr[dev];
     return ZG_OK;

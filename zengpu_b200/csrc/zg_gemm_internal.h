@@ -18,6 +18,9 @@ namespace zg {
 //   TF32X3        per 16-k block one 128-byte row: 16 tf32 hi, 16 tf32 lo
 //   TF32_BF16X2   per 16-k block one 128-byte row: 16 tf32 hi (64 B),
 //                 16 bf16(hi) (32 B), 16 bf16(x - hi) (32 B)
+//   BF16X3        per 32-k block one 128-byte row: 32 bf16(x) (64 B), then
+//                 32 bf16(x - bf16(x)) (64 B); 4 bytes per element, the size
+//                 of the f32 input
 // The interleaved rows let one 128-byte-swizzled TMA box carry every term a
 // stage needs; k beyond K inside the last block is zero.
 struct OperandView {

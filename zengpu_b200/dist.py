@@ -4,9 +4,11 @@ The reference has no collective (its only multi-device op is a HIP peer
 copy, zengpu-hip/src/lib.rs:609-710); large problems here shard naturally:
 
 * GEMM: A and C are split into contiguous M-row blocks, one per rank; every
-  rank needs all of B, so B is broadcast from its owner over NCCL (NVLink /
-  NVSwitch) - the only exchange on the path.  C stays sharded; gather_rows()
-  assembles it only when a caller asks for the whole matrix.
+  rank needs all of B - the only exchange on the path.  By default
+  (ChainedGemm) B is packed once on its owner and carried rank to rank over
+  NVLink by the copy engines while every rank's GEMM already runs; ShardedGemm
+  broadcasts it over NCCL instead.  C stays sharded; gather_rows() assembles
+  it only when a caller asks for the whole matrix.
 * elementwise add / ReLU: contiguous chunks, no collective at all.
 
 torch.distributed supplies the process group (NCCL on GPUs, gloo for the CPU
@@ -14,6 +16,8 @@ tests); the per-shard compute is libzengpu_b200's own kernels.
 """
 from __future__ import annotations
 
+import os
+import time
 from typing import Callable
 
 import torch
@@ -178,6 +182,84 @@ def default_chunk_cols(n: int, k: int, target_bytes: int = 16 << 20, bytes_per_e
     return min(cols, ((n + 255) // 256) * 256)
 
 
+class ChainBroken(RuntimeError):
+    """The B chain can no longer run steps: a neighbouring rank exited, or a
+    step did not finish within the deadline."""
+
+
+def pid_alive(pid: int) -> bool:
+    """True while process `pid` runs on this host (a zombie counts as exited)."""
+    try:
+        os.kill(pid, 0)
+    except ProcessLookupError:
+        return False
+    except PermissionError:
+        return True
+    try:
+        with open(f"/proc/{pid}/stat", "rb") as f:
+            state = f.read().rsplit(b")", 1)[1].split()[0]
+        return state not in (b"Z", b"X")
+    except (OSError, IndexError):
+        return True
+
+
+class ChainGuard:
+    """Host-side failure detection of the B chain, checked before each step is
+    launched so that no step is queued toward a rank that has gone.
+
+    * Neighbours: the chain moves data only between neighbouring ranks of one
+      host (CUDA IPC), so a neighbour that left is one whose process no longer
+      runs (pids exchanged when the chain is built).
+    * Deadline: step e is launched only after step e - 2 (the last step that
+      used the same buffers) completed; a step that does not complete within
+      `deadline_s` means a peer stopped taking part.
+    `events[e]` is any object with query() -> bool (a CUDA event in use, a
+    stand-in in the CPU tests)."""
+
+    def __init__(self, rank: int, pids: list[int], prev: int | None, nxt: int | None,
+                 deadline_s: float = 30.0, alive: Callable[[int], bool] = pid_alive):
+        self.rank, self.pids, self.prev, self.next = rank, list(pids), prev, nxt
+        self.deadline_s = deadline_s
+        self.alive = alive
+        self.events: dict[int, object] = {}
+
+    def gone_neighbours(self) -> list[int]:
+        return [r for r in (self.prev, self.next) if r is not None and not self.alive(self.pids[r])]
+
+    def in_flight(self) -> bool:
+        return any(not ev.query() for ev in self.events.values())
+
+    def check_neighbours(self) -> None:
+        gone = self.gone_neighbours()
+        if gone:
+            raise ChainBroken(f"rank {self.rank}: chain neighbour rank {gone[0]} "
+                              f"(pid {self.pids[gone[0]]}) has exited")
+
+    def wait(self, epoch: int, deadline_s: float | None = None) -> None:
+        """Waits until step `epoch` (if it was launched) completed; raises
+        ChainBroken after the deadline."""
+        ev = self.events.get(epoch)
+        if ev is None:
+            return
+        limit = time.monotonic() + (self.deadline_s if deadline_s is None else deadline_s)
+        pause = 1e-5
+        while not ev.query():
+            if time.monotonic() > limit:
+                raise ChainBroken(f"rank {self.rank}: step {epoch} did not complete within "
+                                  f"{self.deadline_s:g} s (a peer stopped taking part)")
+            time.sleep(pause)
+            pause = min(pause * 2, 1e-3)
+
+    def wait_all(self, deadline_s: float | None = None) -> None:
+        for e in sorted(self.events):
+            self.wait(e, deadline_s)
+
+    def launched(self, epoch: int, ev) -> None:
+        self.events[epoch] = ev
+        for e in [e for e in self.events if e <= epoch - 2]:
+            del self.events[e]
+
+
 class ChainedGemm:
     """C[row0:row1] = epilogue(alpha * A[row0:row1] @ B) on every rank, with B
     carried from rank `src` along the chain src -> src+1 -> ... by the copy
@@ -187,10 +269,22 @@ class ChainedGemm:
     it hop rank to rank over NVLink, and each rank's GEMM waits per output
     tile only for the chunk that tile reads.  No SM is spent on the transfer,
     and no collective library is on the data path.  The process group is used
-    once, to exchange the CUDA IPC handles of the chain buffers."""
+    once, to exchange the CUDA IPC handles of the chain buffers.
+
+    Failures (ChainGuard): before each step, both chain neighbours must still
+    run and step e - 2 must have completed within `deadline_s`.  A neighbour
+    that exited with none of this rank's work in flight ends the chain at
+    once.  A deadline that expires while the neighbours still run opens this
+    rank's waits (zg_bchain_abort) so its queued work drains, then ends the
+    chain.  Either way step() raises ChainBroken and every later step does
+    too; the chain's device memory stays allocated until the process exits,
+    since a neighbour that still runs may yet write into it.  If a neighbour
+    exits while this rank's work is still in flight, that work is not
+    released (it would copy into the exited rank's memory): its streams stay
+    blocked and the process should exit."""
 
     def __init__(self, k: int, n: int, mode: int = 3, group=None, src: int = 0,
-                 chunk_cols: int | None = None, lib=None, ops=None):
+                 chunk_cols: int | None = None, lib=None, ops=None, deadline_s: float = 30.0):
         import ctypes as C
 
         from . import _lib as L
@@ -214,12 +308,12 @@ class ChainedGemm:
         check(self.lib.zg_bchain_create(self.mode, k, n, self.chunk_cols, C.byref(ptr), handle))
         self.chain = ptr
         everyone = [None] * self.world
-        dist.all_gather_object(everyone, (bytes(handle), (self.mode, k, n, self.chunk_cols)),
-                               group=group)
-        if any(cfg != everyone[self.rank][1] for _, cfg in everyone):
+        dist.all_gather_object(everyone, (bytes(handle), (self.mode, k, n, self.chunk_cols),
+                                          os.getpid()), group=group)
+        if any(cfg != everyone[self.rank][1] for _, cfg, _ in everyone):
             self.lib.zg_bchain_destroy(self.chain)
             raise ValueError(f"ChainedGemm: ranks disagree on (mode, k, n, chunk): "
-                             f"{[cfg for _, cfg in everyone]}")
+                             f"{[cfg for _, cfg, _ in everyone]}")
 
         def buf(r):
             return None if r is None else (C.c_uint8 * 64).from_buffer_copy(everyone[r][0])
@@ -229,6 +323,10 @@ class ChainedGemm:
         self.copy_stream = torch.cuda.Stream() if torch.cuda.is_available() else None
         self.epoch = 0
         self._packed_a = None
+        self.guard = ChainGuard(self.rank, [p for _, _, p in everyone], self.prev, self.next,
+                                deadline_s)
+        self.broken: str | None = None
+        self._new_event = torch.cuda.Event  # completion marker of each step
 
     def step(self, a_rows: torch.Tensor, b: torch.Tensor | None, out: torch.Tensor,
              alpha: float = 1.0, bias: torch.Tensor | None = None,
@@ -247,6 +345,15 @@ class ChainedGemm:
             raise ValueError(f"ChainedGemm: the source rank needs B [{self.k}, {self.n}]")
         if bias is not None and (bias.numel() != self.n or not bias.is_contiguous()):
             raise ValueError(f"ChainedGemm: bias must be a contiguous [{self.n}] vector")
+        if self.broken:
+            raise ChainBroken(self.broken)
+        # before anything of step e is queued: both neighbours still run, and
+        # step e - 2, the last user of this step's buffers, has completed
+        try:
+            self.guard.check_neighbours()
+            self.guard.wait(self.epoch - 1)
+        except ChainBroken as exc:
+            self._fail(str(exc))
         # every check is done: from here on each rank enqueues the same step e
         self.epoch += 1
         e = self.epoch & 0xFFFFFFFF
@@ -266,7 +373,33 @@ class ChainedGemm:
         # this rank's buffer of step e is free once its GEMM and its forwarding are done
         compute.wait_stream(self.copy_stream)
         self._check(self.lib.zg_bchain_release(self.chain, e, cs))
+        ev = self._new_event()
+        ev.record(compute)
+        self.guard.launched(self.epoch, ev)
         return out
+
+    def _fail(self, reason: str) -> None:
+        """Ends the chain after a failure found on the host and raises."""
+        if self.guard.in_flight():
+            if self.guard.gone_neighbours():
+                self.broken = (reason + "; this rank's queued steps wait on the exited rank and "
+                               "are not released (they would write into its memory): exit "
+                               "this process")
+                raise ChainBroken(self.broken)
+            # the neighbours still run: open this rank's waits so its queued
+            # work ends (results of those steps are invalid), bounded
+            self._check(self.lib.zg_bchain_abort(self.chain, self.epoch & 0xFFFFFFFF))
+            try:
+                self.guard.wait_all()
+            except ChainBroken as exc:
+                self.broken = f"{reason}; after the abort: {exc}"
+                raise ChainBroken(self.broken) from None
+        # a gate that gave up on the device set the status word: clear it, the
+        # failure is reported here
+        code = self._C.c_uint32(0)
+        self.lib.zg_kernel_status(self._C.byref(code))
+        self.broken = reason
+        raise ChainBroken(reason)
 
     def packed_b(self, epoch: int | None = None) -> tuple[int, int]:
         """(device pointer, bytes) of the packed B^T buffer of a step."""
@@ -277,8 +410,10 @@ class ChainedGemm:
         return p.value, nb.value
 
     def close(self) -> None:
-        """Frees the chain after every rank is done with every step."""
-        if self.chain is None:
+        """Frees the chain after every rank is done with every step (collective:
+        every rank calls it).  A chain that failed keeps its memory (see the
+        class docstring) and is not freed here."""
+        if self.chain is None or self.broken:
             return
         if torch.cuda.is_available():
             torch.cuda.synchronize()

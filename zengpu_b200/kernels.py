@@ -79,6 +79,26 @@ def workspace_for(device: torch.device, nbytes: int) -> torch.Tensor | None:
     return ws
 
 
+def release_workspaces(device: torch.device | int | None = None) -> int:
+    """Drops the cached GEMM scratch tensors (of one device, or of all) and
+    returns how many were dropped.  The cache holds one tensor per (device,
+    stream) that ever ran sgemm, each the size of that stream's largest GEMM,
+    until this is called: code that creates short-lived streams should call it
+    once those streams are done.  Dropping a tensor whose GEMM is still queued
+    is safe: torch's caching allocator hands its memory out again only in the
+    order of the stream it was allocated on (the stream it was cached for)."""
+    if device is None:
+        n = len(_workspaces)
+        _workspaces.clear()
+        return n
+    idx = device if isinstance(device, int) else (
+        device.index if device.index is not None else torch.cuda.current_device())
+    keys = [key for key in _workspaces if key[0] == idx]
+    for key in keys:
+        del _workspaces[key]
+    return len(keys)
+
+
 def sgemm(a: torch.Tensor, b: torch.Tensor, mode: int = GemmMode.TF32X3, alpha: float = 1.0,
           bias: torch.Tensor | None = None, relu: bool = False,
           out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:

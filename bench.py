@@ -57,11 +57,13 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
 # dominant kernel, from one ncu capture of the same workload on a B200:
-#   --set full -k regex:sgemm_tc_kernel on `bench.py --steps 1 --warmup 3 --no-extras`
+#   --metrics dram__bytes_read.sum,dram__bytes_write.sum -k regex:sgemm_tc_pair -s 3 -c 1
+#   on `bench.py --steps 10 --warmup 3 --no-extras` (BF16X3, grouped raster of 8 row-tiles);
+#   the other GEMM modes were captured with the earlier raster of 16 row-tiles;
 #   --section MemoryWorkloadAnalysis -k regex:stream_vec_kernel on the elementwise workload
 # Keyed by the kernel and the per-rank GEMM size (M = N = K) or element count.
 NCU_TRAFFIC = {
-    ("sgemm_tc_pair_kernel<4>", 8192): 4.179e9,
+    ("sgemm_tc_pair_kernel<4>", 8192): 3.681e9,
     ("sgemm_tc_pair_kernel<3>", 8192): 5.642e9,
     ("sgemm_tc_pair_kernel<2>", 8192): 5.999e9,
     ("sgemm_tc_pair_kernel<1>", 8192): 3.105e9,

@@ -8,13 +8,40 @@
 // conflict-free 128-bit load.  A is stored transposed (k-major) in shared
 // memory; tiles are double buffered with register staging: the global loads
 // for tile t+1 are in flight while tile t is multiplied.  Products are
-// accumulated with fmaf (IEEE fma, as GEMM_PTX's fma.rn.f32).
+// accumulated with IEEE fma (round to nearest, as GEMM_PTX's fma.rn.f32), two
+// accumulators per instruction with sm_100's packed fma.rn.f32x2: the
+// accumulators are kept as pairs of rows (acc[2p][j], acc[2p+1][j]), A's
+// fragments load straight into such pairs, and each b[j] is broadcast into a
+// pair before its four packed FMAs.  Every element still sees the same fma
+// sequence in k order, so the result is bit-identical to scalar fmaf, and the
+// FFMA issue slots halve.
 #include <cstdint>
 
 #include "zg_common.cuh"
 
 namespace zg {
 namespace {
+
+// d (pair) += a (pair) * b (pair), lane-wise IEEE fma.rn.
+__device__ __forceinline__ void ffma2(uint64_t& d, uint64_t a, uint64_t b) {
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
+}
+__device__ __forceinline__ uint64_t pair_of(float x) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(x));
+    return r;
+}
+// Two adjacent pairs of floats from shared memory (the clobber keeps the load
+// after the barrier that publishes the tile).
+__device__ __forceinline__ void lds_pairs(uint32_t addr, uint64_t& p0, uint64_t& p1) {
+    asm("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(p0), "=l"(p1) : "r"(addr) : "memory");
+}
+__device__ __forceinline__ float pair_lo(uint64_t p) {
+    return __uint_as_float(static_cast<uint32_t>(p));
+}
+__device__ __forceinline__ float pair_hi(uint64_t p) {
+    return __uint_as_float(static_cast<uint32_t>(p >> 32));
+}
 
 constexpr int BM = 128, BN = 128, BK = 16;
 constexpr int kThreads = 256;
@@ -81,11 +108,13 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
     };
 
-    float acc[8][8];
+    // acc2[p][j] = (acc[2p][j], acc[2p + 1][j]); acc rows i: 4ty + i (i < 4),
+    // 64 + 4ty + i - 4 (i >= 4); columns j: 4tx + j (j < 4), 64 + 4tx + j - 4
+    uint64_t acc2[4][8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int p = 0; p < 4; ++p)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+        for (int j = 0; j < 8; ++j) acc2[p][j] = 0ull;
 
     const int nk = (K + BK - 1) / BK;
     if (nk > 0) {
@@ -98,16 +127,18 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (kt + 1 < nk) load_tile((kt + 1) * BK);
 #pragma unroll
         for (int k = 0; k < BK; ++k) {
-            const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4]);
-            const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][k][64 + ty * 4]);
+            uint64_t a2[4];
+            lds_pairs(smem_u32(&As[buf][k][ty * 4]), a2[0], a2[1]);
+            lds_pairs(smem_u32(&As[buf][k][64 + ty * 4]), a2[2], a2[3]);
             const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 4]);
             const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][k][64 + tx * 4]);
-            const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
             const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+            for (int j = 0; j < 8; ++j) {
+                const uint64_t bb = pair_of(b[j]);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+                for (int p = 0; p < 4; ++p) ffma2(acc2[p][j], a2[p], bb);
+            }
         }
         if (kt + 1 < nk) store_tile(buf ^ 1);
         __syncthreads();
@@ -124,7 +155,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             float v[4];
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
-                float x = __fmul_rn(alpha, acc[i][h * 4 + c]);
+                const uint64_t pr = acc2[i >> 1][h * 4 + c];
+                float x = __fmul_rn(alpha, (i & 1) ? pair_hi(pr) : pair_lo(pr));
                 if (bias && col + c < N) x = __fadd_rn(x, __ldg(bias + col + c));
                 if (relu) x = relu1(x);
                 v[c] = x;

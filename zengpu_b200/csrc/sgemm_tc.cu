@@ -644,43 +644,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
 }
 
 // ---- operand pre-pass ------------------------------------------------------------
-// Writes element (row r, k) of one operand view.  TF32 (S = 1): f32 copy;
-// TF32X3 (S = 2): block kb = k / 16 holds tf32(x) at [kb*32 + j] and
-// tf32(x - hi) at [kb*32 + 16 + j]; TF32_BF16X2 (S = 3): tf32(x) at
-// [kb*32 + j], then 16 bf16(hi) and 16 bf16(x - hi) in the block's last
-// 64 bytes.  j = k % 16.  BF16X3 (S = 4): 32-k blocks of 32 bf16(x) then 32
-// bf16(x - hi).  x = 0 for padding k, so the padding is zero.
-template <int S>
-__device__ __forceinline__ void put_value(float* base, int64_t ld, int64_t r, int k, float x) {
-    float* row = base + r * ld;
-    if (S == 1) {
-        row[k] = x;
-        return;
-    }
-    if (S == 4) {
-        // BF16X3: block kb = k / 32 holds bf16(x) at bf16 index j and
-        // bf16(x - hi) at 32 + j, j = k % 32
-        const __nv_bfloat16 h = __float2bfloat16_rn(x);
-        const float l = __fsub_rn(x, __bfloat162float(h));  // exact
-        __nv_bfloat16* bb = reinterpret_cast<__nv_bfloat16*>(row + (k >> 5) * 32);
-        bb[k & 31] = h;
-        bb[32 + (k & 31)] = __float2bfloat16_rn(l);
-        return;
-    }
-    const float h = to_tf32(x);
-    const float l = __fsub_rn(x, h);  // exact: h is x with its low mantissa bits rounded off
-    float* blk = row + (k >> 4) * 32;
-    const int j = k & 15;
-    blk[j] = h;
-    if (S == 2) {
-        blk[16 + j] = to_tf32(l);
-    } else {
-        __nv_bfloat16* bb = reinterpret_cast<__nv_bfloat16*>(blk + 16);
-        bb[j] = __float2bfloat16_rn(h);
-        bb[16 + j] = __float2bfloat16_rn(l);
-    }
-}
-
+// Layout of one operand view row: TF32 (S = 1): f32 copy; TF32X3 (S = 2):
+// block kb = k / 16 holds tf32(x) at [kb*32 + j] and tf32(x - hi) at
+// [kb*32 + 16 + j]; TF32_BF16X2 (S = 3): tf32(x) at [kb*32 + j], then 16
+// bf16(hi) and 16 bf16(x - hi) in the block's last 64 bytes; j = k % 16.
+// BF16X3 (S = 4): 32-k blocks of 32 bf16(x) then 32 bf16(x - hi).  x = 0 for
+// padding k, so the padding is zero.
 // Four consecutive k (k % 4 == 0) of one row with vector stores.
 template <int S>
 __device__ __forceinline__ void put_value4(float* base, int64_t ld, int64_t r, int k, float4 x) {
@@ -784,12 +753,18 @@ __device__ __forceinline__ void transpose_strip(const float* __restrict__ src, i
         for (int j = 0; j < TK / 8; ++j) tile[b][ty + 8 * j][tx] = r[j];
         __syncthreads();
         if (kt + 1 < kt1) load(kt + 1);
-        // 32 rows n x 64 k: warp ty stores rows ty, ty + 8, ..., each in two 32-k halves
+        // 32 rows n x 64 k: each thread packs four consecutive k of one row n
+        // (two such groups) and writes them with the row pre-pass's vector
+        // stores; the 16 threads of a row cover its 64 k, so a row's output
+        // lines are written whole
 #pragma unroll
-        for (int j = 0; j < TK / 8; ++j) {
-            const int nl = ty + 8 * (j >> 1), kl = (j & 1) * 32 + tx;
+        for (int i = 0; i < 2; ++i) {
+            const int nl = (threadIdx.x >> 4) + 16 * i, kl = (threadIdx.x & 15) * 4;
             const int n = n0 + nl, k = kt * TK + kl;
-            if (n < N && k < kpad) put_value<S>(dst, ldd, n, k, tile[b][kl][nl]);
+            if (n < N && k < kpad)  // kpad is a multiple of 4: k + 3 < kpad too
+                put_value4<S>(dst, ldd, n, k,
+                              make_float4(tile[b][kl][nl], tile[b][kl + 1][nl],
+                                          tile[b][kl + 2][nl], tile[b][kl + 3][nl]));
         }
     }
 }

@@ -738,8 +738,8 @@ def sustained_gemm(torch, dist, g, mode, peaks, peak_src, local_rank,
 
 def strong_scaling(args, torch, dist, zg, K, mode, peaks, rank, local_rank, world,
                    seconds: float = 1.5) -> dict:
-    """North star's strong-scaling case, M = N = 32768, K = 8192, in the bench's
-    mode, at this run's N: A's row blocks over the ranks, B from rank 0 along
+    """The strong-scaling case of the sharded configuration, M = N = 32768,
+    K = 8192, in the bench's mode, at this run's N: A's row blocks over the ranks, B from rank 0 along
     the copy-engine chain.  Every N times at least `seconds` of steps, long
     enough to reach the power-limited clock, so N = 1 and N > 1 compare in the
     same regime.  At N > 1 rank 0 also times the whole problem on its GPU alone

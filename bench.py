@@ -504,14 +504,15 @@ class RowGemm:
     def launches_per_step(self) -> int:
         """This library's kernels per step: chain (rank 0) B pack with chunk
         flags, A pack, GEMM; NCCL: A pack + per panel B pack + GEMM; one GPU:
-        the pre-pass kernels of the mode plus the GEMM."""
+        the pre-pass kernels of the mode plus the GEMM (SIMT: A's transpose
+        when n % 4 == 0, for its TMA-fed kernel)."""
         zg = self.zg
         if self.chain is not None:
             return 3
         if self.sg is not None:
             return 1 + 2 * self.panels
         return {zg.GemmMode.TF32X3: 3, zg.GemmMode.TF32: 2 + (self.k % 4 != 0),
-                zg.GemmMode.SIMT_FP32: 1, zg.GemmMode.TF32_BF16X2: 3,
+                zg.GemmMode.SIMT_FP32: 1 + (self.n % 4 == 0), zg.GemmMode.TF32_BF16X2: 3,
                 zg.GemmMode.BF16X3: 3}[self.mode]
 
     def finish_exchange(self):

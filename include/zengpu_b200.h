@@ -363,13 +363,16 @@ int zg_sscal_f32(float alpha, float *x, uint64_t n, void *stream);
 
 /* Scratch bytes zg_sgemm_f32 needs for (mode, m, n, k): the operand planes
  * the tensor-core kernel reads (tf32 / bf16 planes of A, and of B transposed
- * to K-major; TF32 reads A directly when k is a multiple of 4); SIMT needs
- * none. */
+ * to K-major; TF32 reads A directly when k is a multiple of 4).  SIMT's is
+ * optional: A transposed (k rows of round_up(m, 4) floats) for its TMA-fed
+ * kernel, used when it is given and B is 16-byte aligned with n % 4 == 0;
+ * otherwise SIMT runs its register-staged kernel on A (the same bits). */
 uint64_t zg_sgemm_workspace_bytes(int mode, int m, int n, int k);
 /* C[m,n] = epilogue(alpha * A[m,k] @ B[k,n]), all row-major f32.
  * epilogue: identity, or relu(x + bias[col]) when `bias` is non-NULL and
  * `relu` is 1, or x + bias[col] when `relu` is 0.  `workspace` must hold
- * zg_sgemm_workspace_bytes(...) bytes (may be NULL when that is 0).
+ * zg_sgemm_workspace_bytes(...) bytes (may be NULL when that is 0, and for
+ * SIMT, whose workspace is optional).
  * Replaces GEMM_PTX's entry `main(a,b,c,m,n,k,alpha)` (zengpu-blas/src/level3.rs:35-90). */
 int zg_sgemm_f32(int mode, int m, int n, int k, float alpha, const float *a, const float *b,
                  float *c, const float *bias, int relu, void *workspace,
@@ -378,7 +381,8 @@ int zg_sgemm_f32(int mode, int m, int n, int k, float alpha, const float *a, con
 /* The two halves of zg_sgemm_f32, for callers that reuse operands or time
  * the main kernel alone.  prepare: writes the operand planes of `mode` into
  * `workspace` (tf32 hi/lo of A and B for TF32X3, pitch-padded copies for
- * TF32 when k or n is not a multiple of 4; nothing for SIMT).  compute: runs
+ * TF32 when k or n is not a multiple of 4; A transposed for SIMT when the
+ * workspace and B allow its TMA-fed kernel).  compute: runs
  * the GEMM on planes a previous prepare wrote into the same workspace for the
  * same (mode, m, n, k, a, b); stream order makes the pair safe. */
 int zg_sgemm_prepare(int mode, int m, int n, int k, const float *a, const float *b,
@@ -412,7 +416,8 @@ int zg_sgemm_packed(int mode, int m, int n, int k, float alpha, const void *a_pa
  * fixed 64 MiB scratch array in the library's device image, held on every GPU
  * that loads it until the process exits.  Shapes whose scratch need
  * (zg_sgemm_workspace_bytes) exceeds 64 MiB are rejected with ZG_ERR_DISPATCH
- * (TF32X3 fits up to 2048^3, BF16X3 up to 2880^3).  Allocates nothing.  The
+ * (TF32X3 fits up to 2048^3, BF16X3 up to 2880^3), except in SIMT, which then
+ * runs without its optional workspace.  Allocates nothing.  The
  * first call on each device looks up the array's device address (make it
  * before any stream capture); a call under a new context of that device (after
  * cudaDeviceReset) looks it up again.  All calls share the array: calls that
@@ -431,7 +436,9 @@ int zg_fill_normal_f32(float *x, uint64_t n, uint64_t seed, void *stream);
  * (mode, m, n, k) on the current device ("" for an unknown mode or an empty
  * output), for reports and profiler filters.  The tensor-core modes take the
  * CTA-pair kernel once there is a 256 x 256 tile for every SM pair (unless
- * the environment sets ZENGPU_GEMM_PAIRS=0). */
+ * the environment sets ZENGPU_GEMM_PAIRS=0).  SIMT names its TMA-fed kernel,
+ * the one zg_sgemm_f32 runs with its workspace on 16-byte aligned B with
+ * n % 4 == 0 (without them it runs sgemm_simt_kernel). */
 const char *zg_sgemm_kernel_name(int mode, int m, int n, int k);
 
 /* Reads and clears the device-side status word of the current device:

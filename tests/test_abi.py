@@ -51,7 +51,9 @@ def test_no_device_is_reported_not_crashed():
 
 def test_workspace_bytes():
     lib = zg.load_library()
-    assert lib.zg_sgemm_workspace_bytes(0, 1024, 1024, 1024) == 0
+    # SIMT (optional): A transposed, k rows of round_up(m, 4) floats
+    assert lib.zg_sgemm_workspace_bytes(0, 1024, 1024, 1024) == 1024 * 1024 * 4
+    assert lib.zg_sgemm_workspace_bytes(0, 17, 9, 33) == 256 * ((33 * 20 * 4 + 255) // 256)
     # TF32X3 / TF32_BF16X2: A (m rows) and B transposed (n rows), each 16-k block
     # one 128-byte row of interleaved terms (k padded to 16), 256-byte aligned
     assert lib.zg_sgemm_workspace_bytes(1, 8192, 8192, 8192) == 4 * 8192 * 8192 * 4
@@ -134,7 +136,7 @@ def test_sgemm_kernel_name():
     assert name(3, 8192, 8192, 8192) == "sgemm_tc_pair_kernel<3>"
     assert name(1, 256, 512, 64) == "sgemm_tc_kernel<2>"
     assert name(2, 256, 512, 64) == "sgemm_tc_kernel<1>"
-    assert name(0, 8192, 8192, 8192) == "sgemm_simt_kernel"
+    assert name(0, 8192, 8192, 8192) == "sgemm_simt_tma_kernel"
     assert name(3, 64, 64, 0) == "gemm_k0_kernel"
     assert name(9, 64, 64, 64) == "" and name(3, 0, 64, 64) == ""
 

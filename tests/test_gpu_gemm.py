@@ -113,6 +113,41 @@ def test_odd_shapes(mode, m, n, k):
         assert O.rel_fro(c, O.sgemm(a, b, alpha)) <= max(TOL[mode], 2e-6)
 
 
+@pytest.mark.parametrize("m,n,k", [(300, 520, 72), (1000, 776, 1032), (128, 128, 16), (5, 3, 4)])
+def test_simt_tma_and_register_staged_kernels_agree(m, n, k):
+    """SIMT runs its TMA-fed kernel on A transposed in its workspace when B is
+    16-byte aligned with n % 4 == 0, and the register-staged kernel on A
+    itself otherwise: with the values one float past that boundary, or with
+    no workspace at all.  All give the same bits (ragged M, N and K here)."""
+    a = O.uniform(m * k, 31).reshape(m, k)
+    b = O.uniform(k * n, 32).reshape(k, n)
+    bias = O.uniform(n, 33)
+    ta, tb = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    buf_a = torch.empty(m * k + 1, device="cuda")
+    buf_b = torch.empty(k * n + 1, device="cuda")
+    buf_a[1:] = ta.reshape(-1)
+    buf_b[1:] = tb.reshape(-1)
+    ua, ub = buf_a[1:].view(m, k), buf_b[1:].view(k, n)
+    assert ta.data_ptr() % 16 == 0 and ua.data_ptr() % 16 != 0
+    tbias = torch.from_numpy(bias).cuda()
+    for relu in (False, True):
+        fast = K.sgemm(ta, tb, mode=zg.GemmMode.SIMT_FP32, alpha=-0.75, bias=tbias, relu=relu)
+        slow = K.sgemm(ua, ub, mode=zg.GemmMode.SIMT_FP32, alpha=-0.75, bias=tbias, relu=relu)
+        torch.cuda.synchronize()
+        assert K.kernel_status() == 0
+        np.testing.assert_array_equal(bits(fast.cpu().numpy()), bits(slow.cpu().numpy()))
+        bare = torch.empty((m, n), device="cuda")
+        zg.api.check(zg.load_library().zg_sgemm_f32(
+            int(zg.GemmMode.SIMT_FP32), m, n, k, -0.75, ta.data_ptr(), tb.data_ptr(),
+            bare.data_ptr(), tbias.data_ptr(), int(relu), None, 0,
+            torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(bits(fast.cpu().numpy()), bits(bare.cpu().numpy()))
+        ref = (O.sgemm_bias_relu(a, b, bias, -0.75) if relu
+               else O.sgemm(a, b, -0.75) + bias[None, :])
+        assert O.rel_fro(fast.cpu().numpy(), ref) <= 1e-5
+
+
 @pytest.mark.parametrize("mode", MODES, ids=lambda m: m.name)
 def test_k_zero(mode):
     a = np.zeros((5, 0), np.float32)

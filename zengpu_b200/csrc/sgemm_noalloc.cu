@@ -13,8 +13,10 @@
 // The scratch array below is kNoAllocScratchBytes (64 MiB) on every GPU where
 // this file's module is loaded, held until the process exits.  It bounds the
 // shapes the entry point accepts: zg_sgemm_workspace_bytes(mode, m, n, k)
-// must not exceed it (TF32X3 fits up to 2048 x 2048 x 2048; SIMT needs none).
-// Larger shapes are rejected with ZG_ERR_DISPATCH and nothing is launched.
+// must not exceed it (TF32X3 fits up to 2048 x 2048 x 2048).  Larger shapes
+// are rejected with ZG_ERR_DISPATCH and nothing is launched, except in SIMT,
+// whose workspace (A transposed, up to 4096 x 4096) is optional: beyond the
+// array it runs without one, on the register-staged kernel.
 //
 // Host code must not pass the array's name to a kernel: on the host it is
 // only a stand-in symbol, not a device address.  The first call on each
@@ -107,7 +109,10 @@ extern "C" int zg_sgemm_f32_noalloc(int mode, int m, int n, int k, float alpha, 
     if (m < 0 || n < 0 || k < 0)
         return set_error(ZG_ERR_DISPATCH, "zg_sgemm_f32_noalloc: negative shape %d x %d x %d", m,
                          n, k);
-    const uint64_t need = zg_sgemm_workspace_bytes(mode, m, n, k);
+    uint64_t need = zg_sgemm_workspace_bytes(mode, m, n, k);
+    // SIMT's workspace (A transposed) is optional: without it, it runs the
+    // register-staged kernel on A itself
+    if (mode == ZG_GEMM_SIMT_FP32 && need > kNoAllocScratchBytes) need = 0;
     if (need > kNoAllocScratchBytes)
         return set_error(ZG_ERR_DISPATCH,
                          "zg_sgemm_f32_noalloc: %d x %d x %d (mode %d) needs %llu bytes of "

@@ -15,11 +15,17 @@
 // pair before its four packed FMAs.  Every element still sees the same fma
 // sequence in k order, so the result is bit-identical to scalar fmaf, and the
 // FFMA issue slots halve.
+#include <atomic>
 #include <cstdint>
+#include <cstring>
 
 #include "zg_common.cuh"
 
 namespace zg {
+
+// Device status word of the SIMT SGEMM's bounded waits (read by zg_kernel_status).
+__device__ uint32_t g_simt_status = 0;
+
 namespace {
 
 // d (pair) += a (pair) * b (pair), lane-wise IEEE fma.rn.
@@ -183,9 +189,170 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 }
 
+// ---- TMA-fed kernel (A transposed by a pre-pass) ------------------------------------
+// The same 128 x 128 tile, 8 x 8 thread tile and inner loop, but both operands
+// arrive by TMA as 16 k rows of 128 floats: B as it lies in global memory and
+// A from its transposed copy (A^T: k rows of m, written by the caller's
+// pre-pass), so A's stage has the k-major layout the inner loop reads without
+// any transposing store.  Stages sit in a four-deep ring of shared memory;
+// consumer warps wait on a stage's mbarrier, multiply it and release it, and
+// thread 0 refills each stage one tile after every warp is done with it, so
+// there is no block barrier, no register staging and no global load in the
+// multiply loop.  TMA writes zeros beyond the matrix (rows, columns, k), as
+// the register-staged kernel does, so every element sees the same fma
+// sequence and both kernels give the same bits.
+constexpr int kTStages = 4;
+constexpr int kTThreads = 256;
+constexpr int kTStageFloats = BK * BM;                     // per operand per stage
+constexpr uint32_t kTStageBytes = 2 * kTStageFloats * 4;   // A^T and B: 16 KB
+constexpr int kTSmemBytes = kTStages * kTStageBytes + 1024 /*align*/ + 2 * kTStages * 8;
+static_assert(BM == BN, "A^T and B stages share one shape");
+
+struct SimtMaps {
+    CUtensorMap at;  // A^T: M columns x K rows, box 128 x 16
+    CUtensorMap b;   // B:   N columns x K rows, box 128 x 16
+};
+
+__global__ void __launch_bounds__(kTThreads, 2)
+    sgemm_simt_tma_kernel(const __grid_constant__ SimtMaps maps, int M, int N, int K, float alpha,
+                          float* __restrict__ C, int64_t ldc, const float* __restrict__ bias,
+                          int relu, int vec_c) {
+    uint32_t* status = &g_simt_status;
+    extern __shared__ uint8_t smem_raw[];
+    float* smem = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                           ~uintptr_t(1023));
+    float* As = smem;                                  // [stage][BK][BM]
+    float* Bs = smem + kTStages * kTStageFloats;       // [stage][BK][BN]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kTStages * kTStageFloats);
+    uint64_t* empty = full + kTStages;
+
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int nk = (K + BK - 1) / BK;
+    const bool producer = tid == 0;
+
+    auto issue = [&](int t) {
+        const int s = t % kTStages;
+        mbar_arrive_expect_tx(&full[s], kTStageBytes);
+        tma_load_2d(As + s * kTStageFloats, &maps.at, m0, t * BK, &full[s]);
+        tma_load_2d(Bs + s * kTStageFloats, &maps.b, n0, t * BK, &full[s]);
+    };
+    int issued = 0;
+    if (producer) {
+        for (int s = 0; s < kTStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kTThreads / 32);  // one arrive per warp
+        }
+        fence_mbar_init();
+        prefetch_tensormap(&maps.at);
+        prefetch_tensormap(&maps.b);
+        for (; issued < kTStages - 1 && issued < nk; ++issued) issue(issued);
+    }
+    __syncthreads();
+
+    // acc2[p][j] = (acc[2p][j], acc[2p + 1][j]); acc rows i: 4ty + i (i < 4),
+    // 64 + 4ty + i - 4 (i >= 4); columns j: 4tx + j (j < 4), 64 + 4tx + j - 4
+    uint64_t acc2[4][8];
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc2[p][j] = 0ull;
+
+    bool ok = true;
+    for (int kt = 0; kt < nk; ++kt) {
+        const int s = kt % kTStages;
+        // the warp gives up together, so no lane multiplies a stage that never came
+        const bool got =
+            mbar_wait_bounded(&full[s], (kt / kTStages) & 1, status, kErrSimtConsumer);
+        if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
+        }
+        const float* as = As + s * kTStageFloats;
+        const float* bs = Bs + s * kTStageFloats;
+#pragma unroll
+        for (int k = 0; k < BK; ++k) {
+            uint64_t a2[4];
+            lds_pairs(smem_u32(as + k * BM + ty * 4), a2[0], a2[1]);
+            lds_pairs(smem_u32(as + k * BM + 64 + ty * 4), a2[2], a2[3]);
+            const float4 b0 = *reinterpret_cast<const float4*>(bs + k * BN + tx * 4);
+            const float4 b1 = *reinterpret_cast<const float4*>(bs + k * BN + 64 + tx * 4);
+            const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint64_t bb = pair_of(b[j]);
+#pragma unroll
+                for (int p = 0; p < 4; ++p) ffma2(acc2[p][j], a2[p], bb);
+            }
+        }
+        // every lane's reads of the stage come before the warp frees it
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        // thread 0: tile kt + 3 goes into the stage of tile kt - 1 once every
+        // warp has released that stage
+        bool pok = true;
+        if (producer && issued < nk) {
+            const int t = issued;
+            if (t >= kTStages)
+                pok = mbar_wait_bounded(&empty[t % kTStages], ((t / kTStages) - 1) & 1, status,
+                                        kErrSimtProducer);
+            if (pok) {
+                issue(t);
+                ++issued;
+            }
+        }
+        if (!__all_sync(0xffffffffu, pok)) {
+            ok = false;
+            break;
+        }
+    }
+    // No copy of this block may still be landing when it exits.
+    if (producer)
+        for (int i = issued > kTStages ? issued - kTStages : 0; i < issued; ++i)
+            mbar_wait_bounded(&full[i % kTStages], (i / kTStages) & 1, status, kErrSimtDrain);
+    if (!ok) return;
+
+    // Epilogue: c = alpha*acc, then + bias[col], then ReLU, each rounded.
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+        if (row >= M) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int col = n0 + h * 64 + tx * 4;
+            float v[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint64_t pr = acc2[i >> 1][h * 4 + c];
+                float x = __fmul_rn(alpha, (i & 1) ? pair_hi(pr) : pair_lo(pr));
+                if (bias && col + c < N) x = __fadd_rn(x, __ldg(bias + col + c));
+                if (relu) x = relu1(x);
+                v[c] = x;
+            }
+            float* dst = C + row * ldc + col;
+            if (vec_c && col + 3 < N) {
+                *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    if (col + c < N) dst[c] = v[c];
+            }
+        }
+    }
+}
+
 }  // namespace
 
-// Launches the SIMT SGEMM on `stream`; shapes already validated by the caller.
+cudaError_t take_simt_status(uint32_t* v) {
+    uint32_t zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(v, g_simt_status, sizeof(*v));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_simt_status, &zero, sizeof(zero));
+    return e;
+}
+
+// Launches the register-staged SIMT SGEMM on `stream`; shapes already
+// validated by the caller.
 int launch_sgemm_simt(int M, int N, int K, float alpha, const float* A, int64_t lda,
                       const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias,
                       int relu, cudaStream_t stream) {
@@ -206,6 +373,35 @@ int launch_sgemm_simt(int M, int N, int K, float alpha, const float* A, int64_t 
         sgemm_simt_kernel<false, false><<<grid, kThreads, 0, stream>>>(M, N, K, alpha, A, lda, B, ldb, C,
                                                                        ldc, bias, relu, vc);
     return cuda_status(cudaGetLastError(), "sgemm_simt");
+}
+
+// Launches the TMA-fed SIMT SGEMM on A^T (K rows of M floats, pitch ldat) and
+// B (K rows of N floats, pitch ldb): both 16-byte aligned with pitches of a
+// multiple of 4 floats, K > 0 (the caller checks).
+int launch_sgemm_simt_at(int M, int N, int K, float alpha, const float* At, int64_t ldat,
+                         const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias,
+                         int relu, cudaStream_t stream) {
+    const int vc = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
+    SimtMaps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    int rc = encode_f32_map(&maps.at, At, M, K, ldat, BM, BK, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!rc) rc = encode_f32_map(&maps.b, B, N, K, ldb, BN, BK, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    // the dynamic shared-memory opt-in, once per device
+    static std::atomic<uint64_t> attr_done{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_done.load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(
+            sgemm_simt_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemBytes);
+        if (e != cudaSuccess) return cuda_status(e, "sgemm_simt_tma smem attribute");
+        attr_done.fetch_or(bit);
+    }
+    dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+    sgemm_simt_tma_kernel<<<grid, kTThreads, kTSmemBytes, stream>>>(maps, M, N, K, alpha, C, ldc,
+                                                                    bias, relu, vc);
+    return cuda_status(cudaGetLastError(), "sgemm_simt_tma");
 }
 
 }  // namespace zg

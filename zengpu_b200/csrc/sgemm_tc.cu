@@ -73,6 +73,9 @@ __device__ uint32_t g_status = 0;
 int launch_sgemm_simt(int M, int N, int K, float alpha, const float* A, int64_t lda,
                       const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias,
                       int relu, cudaStream_t stream);
+int launch_sgemm_simt_at(int M, int N, int K, float alpha, const float* At, int64_t ldat,
+                         const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias,
+                         int relu, cudaStream_t stream);
 
 namespace {
 
@@ -862,20 +865,7 @@ int sm_count() {
 // {32 units (128 B), box_rows}, 128-byte swizzle.
 int encode_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld,
                uint32_t box_rows) {
-    auto fn = get_encode_fn();
-    if (!fn) return set_error(ZG_ERR_BACKEND, "cuTensorMapEncodeTiled unavailable");
-    cuuint64_t dims[2] = {cols, rows};
-    cuuint64_t strides[1] = {ld * 4};
-    cuuint32_t box[2] = {32, box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims,
-                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS)
-        return set_error(ZG_ERR_BACKEND, "cuTensorMapEncodeTiled failed (%d): %llux%llu ld=%llu",
-                         static_cast<int>(r), (unsigned long long)rows, (unsigned long long)cols,
-                         (unsigned long long)ld);
-    return ZG_OK;
+    return encode_f32_map(map, base, cols, rows, ld, 32, box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 unsigned row_grid(int rows) {
@@ -1056,6 +1046,24 @@ int run_tc(const GemmOperands& op, int M, int N, int K, float alpha, float* C, i
 
 }  // namespace
 
+int encode_f32_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld,
+                   uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+    auto fn = get_encode_fn();
+    if (!fn) return set_error(ZG_ERR_BACKEND, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld * 4};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(ZG_ERR_BACKEND, "cuTensorMapEncodeTiled failed (%d): %llux%llu ld=%llu",
+                         static_cast<int>(r), (unsigned long long)rows, (unsigned long long)cols,
+                         (unsigned long long)ld);
+    return ZG_OK;
+}
+
 // ---- GEMM building blocks (shared with the packed API and the host GEMM) -----------
 bool gemm_a_needs_planes(int mode, int K) {
     return mode == ZG_GEMM_TF32X3 || mode == ZG_GEMM_TF32_BF16X2 || mode == ZG_GEMM_BF16X3 ||
@@ -1138,9 +1146,25 @@ struct WsLayout {
     bool a_planes, b_planes;
 };
 
+// SIMT's workspace is optional: A transposed (k rows of round_up(m, 4)
+// floats) for the TMA-fed kernel.  Without it, or with B not 16-byte aligned
+// or n % 4 != 0, SIMT runs the register-staged kernel on A itself (same bits).
+uint64_t simt_at_bytes(int m, int k) {
+    return round_up(static_cast<uint64_t>(k) * round_up(m, 4) * 4, 256);
+}
+bool simt_uses_at(int m, int n, int k, const float* b, const void* ws, uint64_t ws_bytes) {
+    return m > 0 && n > 0 && k > 0 && ws && ws_bytes >= simt_at_bytes(m, k) &&
+           (reinterpret_cast<uintptr_t>(ws) & 255u) == 0 && n % 4 == 0 && aligned16(b) &&
+           k <= 65535 * 32;  // the transposing pre-pass grid
+}
+
 WsLayout ws_layout(int mode, int m, int n, int k) {
     WsLayout w{0, 0, false, false};
     if (m <= 0 || n <= 0 || k <= 0 || !valid_mode(mode)) return w;
+    if (mode == ZG_GEMM_SIMT_FP32) {
+        w.total = simt_at_bytes(m, k);
+        return w;
+    }
     w.a_planes = gemm_a_needs_planes(mode, k);
     w.b_planes = gemm_b_needs_planes(mode);
     w.b_off = w.a_planes ? gemm_planes_bytes(mode, m, k) : 0;
@@ -1172,7 +1196,7 @@ int check_gemm_args(int mode, int m, int n, int k, const float* a, const float* 
     }
     if ((need_c && !c) || (k > 0 && (!a || !b)))
         return set_error(ZG_ERR_DISPATCH, "sgemm: null operand pointer");
-    const uint64_t need = ws_layout(mode, m, n, k).total;
+    const uint64_t need = mode == ZG_GEMM_SIMT_FP32 ? 0 : ws_layout(mode, m, n, k).total;
     if (need > 0 && (!workspace || workspace_bytes < need))
         return set_error(ZG_ERR_DISPATCH,
                          "sgemm: workspace of %llu bytes needed for %d x %d x %d, got %llu",
@@ -1233,6 +1257,14 @@ extern "C" int zg_sgemm_prepare(int mode, int m, int n, int k, const float* a, c
                              &trivial);
     if (rc || trivial || k == 0) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (mode == ZG_GEMM_SIMT_FP32) {
+        if (!simt_uses_at(m, n, k, b, workspace, workspace_bytes)) return ZG_OK;
+        // A^T: the f32 transposing pre-pass with A's m rows as its k
+        OperandView at;
+        at.p = workspace;
+        at.ld = round_up(m, 4);
+        return launch_prep_transpose(ZG_GEMM_TF32, a, m, k, k, at, s);
+    }
     const GemmOperands op =
         operands_in_workspace(mode, m, n, k, a, b, static_cast<uint8_t*>(workspace));
     if ((rc = gemm_prep_a(mode, m, k, a, k, op.a, s))) return rc;
@@ -1247,6 +1279,9 @@ extern "C" int zg_sgemm_compute(int mode, int m, int n, int k, float alpha, cons
     if (rc || trivial) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (k == 0) return launch_k0(m, n, alpha, c, n, bias, relu, s);
+    if (mode == ZG_GEMM_SIMT_FP32 && simt_uses_at(m, n, k, b, workspace, workspace_bytes))
+        return launch_sgemm_simt_at(m, n, k, alpha, static_cast<const float*>(workspace),
+                                    round_up(m, 4), b, n, c, n, bias, relu, s);
     const GemmOperands op = operands_in_workspace(
         mode, m, n, k, a, b, static_cast<uint8_t*>(const_cast<void*>(workspace)));
     return gemm_run(op, m, n, k, alpha, c, n, bias, relu, s);
@@ -1312,7 +1347,7 @@ extern "C" int zg_sgemm_packed(int mode, int m, int n, int k, float alpha, const
 extern "C" const char* zg_sgemm_kernel_name(int mode, int m, int n, int k) {
     if (!valid_mode(mode) || m <= 0 || n <= 0 || k < 0) return "";
     if (k == 0) return "gemm_k0_kernel";
-    if (mode == ZG_GEMM_SIMT_FP32) return "sgemm_simt_kernel";
+    if (mode == ZG_GEMM_SIMT_FP32) return "sgemm_simt_tma_kernel";
     static const char* const pair[] = {"", "sgemm_tc_pair_kernel<1>", "sgemm_tc_pair_kernel<2>",
                                        "sgemm_tc_pair_kernel<3>", "sgemm_tc_pair_kernel<4>"};
     static const char* const single[] = {"", "sgemm_tc_kernel<1>", "sgemm_tc_kernel<2>",
@@ -1322,9 +1357,10 @@ extern "C" const char* zg_sgemm_kernel_name(int mode, int m, int n, int k) {
 }
 
 extern "C" int zg_kernel_status(uint32_t* code) {
-    uint32_t v = 0, zero = 0;
+    uint32_t v = 0, zero = 0, simt = 0;
     cudaError_t e = cudaMemcpyFromSymbol(&v, g_status, sizeof(v));
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_status, &zero, sizeof(zero));
-    if (code) *code = v;
+    if (e == cudaSuccess) e = take_simt_status(&simt);
+    if (code) *code = v | simt;
     return cuda_status(e, "zg_kernel_status");
 }

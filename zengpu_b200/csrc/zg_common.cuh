@@ -18,6 +18,9 @@ enum : uint32_t {
     kErrTcEpilogue = 1u << 2,
     kErrTcDrain = 1u << 3,
     kErrTcGate = 1u << 4,  // a B chunk never arrived (multi-GPU arrival gate)
+    kErrSimtProducer = 1u << 5,  // TMA-fed SIMT SGEMM: a stage was never freed
+    kErrSimtConsumer = 1u << 6,  // ... a stage never arrived
+    kErrSimtDrain = 1u << 7,     // ... an issued copy never landed before exit
 };
 
 // Every on-device wait gives up after this long and reports instead of
@@ -297,4 +300,10 @@ namespace zg {
 // Records `msg` as the calling thread's last error and returns `code`.
 int set_error(int code, const char* fmt, ...);
 int cuda_status(cudaError_t e, const char* what);
+// 2-D tiled TMA map over `rows` rows of `cols` f32, pitch `ld` floats, box
+// {box_cols, box_rows}; out-of-range elements load as zero.
+int encode_f32_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld,
+                   uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle);
+// Reads and clears the SIMT SGEMM's device status word (bits kErrSimt*).
+cudaError_t take_simt_status(uint32_t* v);
 }  // namespace zg

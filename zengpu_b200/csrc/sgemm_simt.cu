@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(kTThreads, 2)
 cudaError_t take_simt_status(uint32_t* v) {
     uint32_t zero = 0;
     cudaError_t e = cudaMemcpyFromSymbol(v, g_simt_status, sizeof(*v));
-    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_simt_status, &zero, sizeof(zero));
+    if (e == cudaSuccess && *v) e = cudaMemcpyToSymbol(g_simt_status, &zero, sizeof(zero));
     return e;
 }
 

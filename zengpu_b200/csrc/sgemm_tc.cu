@@ -1358,8 +1358,9 @@ extern "C" const char* zg_sgemm_kernel_name(int mode, int m, int n, int k) {
 
 extern "C" int zg_kernel_status(uint32_t* code) {
     uint32_t v = 0, zero = 0, simt = 0;
+    // clear only a word that is set: the common case is two 4-byte reads
     cudaError_t e = cudaMemcpyFromSymbol(&v, g_status, sizeof(v));
-    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_status, &zero, sizeof(zero));
+    if (e == cudaSuccess && v) e = cudaMemcpyToSymbol(g_status, &zero, sizeof(zero));
     if (e == cudaSuccess) e = take_simt_status(&simt);
     if (code) *code = v | simt;
     return cuda_status(e, "zg_kernel_status");

@@ -84,6 +84,24 @@ def test_sgemm_argument_errors_are_dispatch():
     assert "workspace" in L.last_error()
 
 
+def test_simt_workspace_is_optional():
+    """SIMT states a workspace (A transposed, for its TMA-fed kernel) but runs
+    without one: a call with none passes the argument checks, where every
+    other fp32-class mode rejects it (no GPU here, so the SIMT call then fails
+    at the launch, not at the checks)."""
+    if zg.device_count() > 0:
+        pytest.skip("a GPU is visible: the SIMT call would launch on placeholder pointers")
+    lib = zg.load_library()
+    fake = C.c_void_p(0x1000)
+    assert lib.zg_sgemm_workspace_bytes(0, 64, 64, 64) > 0
+    rc = lib.zg_sgemm_f32(0, 64, 64, 64, 1.0, fake, fake, fake, None, 0, None, 0, None)
+    assert rc != zg.api.Dispatch.code and "workspace" not in L.last_error()
+    for mode in (1, 3, 4):
+        assert lib.zg_sgemm_f32(mode, 64, 64, 64, 1.0, fake, fake, fake, None, 0, None, 0,
+                                None) == zg.api.Dispatch.code
+        assert "workspace" in L.last_error()
+
+
 def test_elementwise_argument_errors():
     lib = zg.load_library()
     assert lib.zg_add_f32(None, None, None, 0, None) == 0  # empty is a no-op

@@ -3,7 +3,8 @@ allocate device memory when they call (a framework that owns all of HBM in
 its own pool, a latency-critical loop that cannot pay for cudaMalloc's
 device-wide synchronisation, code inside an allocator callback).  It must
 match zg_sgemm_f32 with a caller workspace, on two calls in a row, allocate
-nothing, and reject shapes beyond its 64 MiB static scratch.
+nothing, and reject shapes beyond its 64 MiB static scratch (except in SIMT,
+whose workspace is optional).
 
 This file is collected last on purpose, so that a stop-at-first-failure run
 has already run every other test; it also passes alone in a fresh process."""
@@ -116,3 +117,25 @@ def test_noalloc_rejects_shapes_beyond_the_static_scratch():
     ref = K.sgemm(a2, b2, mode=zg.GemmMode.TF32X3)
     torch.cuda.synchronize()
     assert O.rel_fro(c2.cpu().numpy(), ref.cpu().numpy()) <= 1e-5
+
+
+def test_noalloc_simt_beyond_the_scratch_runs_without_it():
+    """SIMT's workspace (A transposed, 4 bytes per m * k element) is optional:
+    a shape whose transposed A does not fit the 64 MiB array runs on the
+    register-staged kernel instead of being rejected, with the same bits as the
+    workspace path, twice in a row and without allocating."""
+    torch.cuda.set_device(0)
+    m, n, k = 4160, 256, 4096
+    mode = zg.GemmMode.SIMT_FP32
+    assert K.workspace_bytes(mode, m, n, k) > 64 << 20
+    a, b, bias = _inputs(m, n, k, 70)
+    ref = K.sgemm(a, b, mode=mode, alpha=-0.25, bias=bias, relu=True)
+    for _ in range(2):
+        c = torch.full((m, n), float("nan"), device="cuda")
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
+        assert _noalloc(a, b, c, mode, alpha=-0.25, bias=bias, relu=True) == 0, L.last_error()
+        torch.cuda.synchronize()
+        assert K.kernel_status() == 0
+        assert torch.cuda.mem_get_info()[0] == free_before
+        assert torch.equal(c.view(torch.int32), ref.view(torch.int32))

@@ -351,3 +351,47 @@ def test_second_device_in_one_process(mode):
     assert np.array_equal(bits(outs[0]), bits(outs[2]))
     ref = O.dgemm_tile(a, b, 0, 0, 128, 128)
     assert O.rel_fro(outs[1][:128, :128], ref) <= TOL[mode] * 1.5
+
+
+_TAIL_SCRIPT = r"""
+import sys, numpy as np, torch
+import zengpu_b200 as zg
+from zengpu_b200 import kernels as K
+mode, m, n, k, out = int(sys.argv[1]), int(sys.argv[2]), int(sys.argv[3]), int(sys.argv[4]), sys.argv[5]
+a = K.fill_uniform(torch.empty((m, k), device="cuda"), 81)
+b = K.fill_uniform(torch.empty((k, n), device="cuda"), 82)
+bias = K.fill_uniform(torch.empty(n, device="cuda"), 83, -0.1, 0.1)
+c = K.sgemm(a, b, mode=mode, alpha=0.5, bias=bias, relu=True)
+torch.cuda.synchronize()
+assert K.kernel_status() == 0
+np.save(out, c.cpu().numpy())
+"""
+
+
+@pytest.mark.parametrize("mode", [zg.GemmMode.BF16X3, zg.GemmMode.TF32X3, zg.GemmMode.TF32,
+                                  zg.GemmMode.TF32_BF16X2], ids=lambda m: m.name)
+def test_tail_split_keeps_bits(mode, tmp_path):
+    """4096 x 4096 output tiles: 256 CTA-pair tiles make 3 waves of 74 and a
+    last wave of 34, which runs as 68 half-width (256 x 128) units.  The same
+    GEMM with whole tiles only (ZENGPU_GEMM_TAIL_SPLIT=0, a fresh process)
+    gives the same bits, and both meet the bar on sampled blocks."""
+    import os
+    import subprocess
+    import sys
+    m = n = 4096
+    k = 1024
+    outs = []
+    for flag in ("1", "0"):
+        path = tmp_path / f"c{flag}.npy"
+        env = dict(os.environ, ZENGPU_GEMM_TAIL_SPLIT=flag)
+        subprocess.run([sys.executable, "-c", _TAIL_SCRIPT, str(int(mode)), str(m), str(n),
+                        str(k), str(path)], env=env, check=True, timeout=600)
+        outs.append(np.load(path))
+    np.testing.assert_array_equal(bits(outs[0]), bits(outs[1]))
+    a = K.fill_uniform(torch.empty((m, k), device="cuda"), 81).cpu().numpy()
+    b = K.fill_uniform(torch.empty((k, n), device="cuda"), 82).cpu().numpy()
+    bias = K.fill_uniform(torch.empty(n, device="cuda"), 83, -0.1, 0.1).cpu().numpy()
+    # a block of a whole tile and blocks of the last wave's tiles (columns of both halves)
+    for r0, c0 in [(0, 0), (m - 128, n - 256), (m - 128, n - 128)]:
+        ref = np.maximum(0.5 * O.dgemm_tile(a, b, r0, c0, 128, 128) + bias[c0:c0 + 128], 0)
+        assert O.rel_fro(outs[0][r0:r0 + 128, c0:c0 + 128], ref) <= TOL[mode]

@@ -46,7 +46,8 @@
 //               drain and store overlap the next tile's MMAs.
 // Problems with a 256 x 256 tile for every SM pair run the CTA-pair variant
 // (sgemm_tc_pair_kernel: tcgen05 cta_group::2, M = 256, six 32 KB stages per
-// CTA).  A GemmGate lets a GEMM start while its B^T rows are still arriving
+// CTA); when its last wave would occupy at most half of the pairs, that wave's
+// tiles run as 256 x 128 halves (N = 128 MMAs), one per pair.  A GemmGate lets a GEMM start while its B^T rows are still arriving
 // from another GPU: the producer waits for the chunk flag of each tile's B
 // rows before loading them.
 // Every mbarrier and flag wait is bounded (zg_common.cuh); an expiry sets a
@@ -105,6 +106,7 @@ struct TcCfg {
 struct TcMaps {
     CUtensorMap a;
     CUtensorMap b;
+    CUtensorMap b_half;  // CTA pairs: B^T in 64-row boxes, for the half-width tail units
 };
 
 // UMMA shared-memory descriptor (sm100): start, leading / stride byte
@@ -407,38 +409,45 @@ constexpr uint32_t kIdescShapePair =
     (static_cast<uint32_t>(PBN >> 3) << 17) | (static_cast<uint32_t>(PBM >> 4) << 24);
 constexpr uint32_t kIdescTf32Pair = (1u << 4) | (2u << 7) | (2u << 10) | kIdescShapePair;
 constexpr uint32_t kIdescBf16Pair = (1u << 4) | (1u << 7) | (1u << 10) | kIdescShapePair;
+// N = 128: the halves of the tiles of the last, partial wave (see launch_tc_pair).
+constexpr uint32_t kIdescShapePairHalf =
+    (static_cast<uint32_t>((PBN / 2) >> 3) << 17) | (static_cast<uint32_t>(PBM >> 4) << 24);
+constexpr uint32_t kIdescTf32PairHalf = (1u << 4) | (2u << 7) | (2u << 10) | kIdescShapePairHalf;
+constexpr uint32_t kIdescBf16PairHalf = (1u << 4) | (1u << 7) | (1u << 10) | kIdescShapePairHalf;
 
 template <int S>
 __device__ __forceinline__ void issue_stage_pair(uint32_t d_tmem, uint32_t stage_base,
-                                                 bool first) {
+                                                 bool first, bool half) {
     const uint32_t a = stage_base, b = stage_base + PairCfg<S>::A_BYTES;
     auto d = [](uint32_t addr) { return umma_desc(addr, 16, 1024, 2); };
+    const uint32_t idesc_bf16 = half ? kIdescBf16PairHalf : kIdescBf16Pair;
+    const uint32_t idesc_tf32 = half ? kIdescTf32PairHalf : kIdescTf32Pair;
     uint32_t acc = first ? 0u : 1u;
     if (S == 4) {
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk) {
             const uint32_t ko = kk * 32;
-            mma_f16_ss_pair(d_tmem, d(a + 64 + ko), d(b + ko), kIdescBf16Pair, acc);
+            mma_f16_ss_pair(d_tmem, d(a + 64 + ko), d(b + ko), idesc_bf16, acc);
             acc = 1u;
-            mma_f16_ss_pair(d_tmem, d(a + ko), d(b + 64 + ko), kIdescBf16Pair, 1u);
-            mma_f16_ss_pair(d_tmem, d(a + ko), d(b + ko), kIdescBf16Pair, 1u);
+            mma_f16_ss_pair(d_tmem, d(a + ko), d(b + 64 + ko), idesc_bf16, 1u);
+            mma_f16_ss_pair(d_tmem, d(a + ko), d(b + ko), idesc_bf16, 1u);
         }
         return;
     }
     if (S == 3) {
-        mma_f16_ss_pair(d_tmem, d(a + 96), d(b + 64), kIdescBf16Pair, acc);
+        mma_f16_ss_pair(d_tmem, d(a + 96), d(b + 64), idesc_bf16, acc);
         acc = 1u;
-        mma_f16_ss_pair(d_tmem, d(a + 64), d(b + 96), kIdescBf16Pair, 1u);
+        mma_f16_ss_pair(d_tmem, d(a + 64), d(b + 96), idesc_bf16, 1u);
     }
 #pragma unroll
     for (int kk = 0; kk < (S == 1 ? 4 : 2); ++kk) {
         const uint32_t ko = kk * 32;
         if (S == 2) {
-            mma_tf32_ss_pair(d_tmem, d(a + 64 + ko), d(b + ko), kIdescTf32Pair, acc);
+            mma_tf32_ss_pair(d_tmem, d(a + 64 + ko), d(b + ko), idesc_tf32, acc);
             acc = 1u;
-            mma_tf32_ss_pair(d_tmem, d(a + ko), d(b + 64 + ko), kIdescTf32Pair, 1u);
+            mma_tf32_ss_pair(d_tmem, d(a + ko), d(b + 64 + ko), idesc_tf32, 1u);
         }
-        mma_tf32_ss_pair(d_tmem, d(a + ko), d(b + ko), kIdescTf32Pair, acc);
+        mma_tf32_ss_pair(d_tmem, d(a + ko), d(b + ko), idesc_tf32, acc);
         acc = 1u;
     }
 }
@@ -447,7 +456,8 @@ template <int S>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     sgemm_tc_pair_kernel(const __grid_constant__ TcMaps maps, int M, int N, int K, float alpha,
                          float* __restrict__ C, int64_t ldc, const float* __restrict__ bias,
-                         int relu, int vec_c, const GemmGate gate) {
+                         int relu, int vec_c, const GemmGate gate, int full_units,
+                         int split) {
     using Cfg = PairCfg<S>;
     constexpr int BK = Cfg::BK, STAGES = Cfg::STAGES;
 
@@ -474,6 +484,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         tile_coords(t, mt, nt, mi, ni);
         m0 = mi * PBM;
         n0 = ni * PBN;
+    };
+    // Unit u: tile u while u < full_units; after that (split == 2) the column
+    // halves of the remaining tiles, tile full_units + (u - full_units) / 2,
+    // columns [n0 + 128 h, n0 + 128 h + 128) for h = (u - full_units) % 2.
+    const int num_units = full_units + (num_tiles - full_units) * split;
+    auto unit_half = [&](int u) { return split > 1 && u >= full_units; };
+    auto unit_origin = [&](int u, int& m0, int& n0) {
+        if (!unit_half(u)) {
+            tile_origin(u, m0, n0);
+            return;
+        }
+        tile_origin(full_units + (u - full_units) / split, m0, n0);
+        n0 += ((u - full_units) % split) * (PBN / 2);
     };
 
     if (threadIdx.x == 0) {
@@ -503,10 +526,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         if (lane == 0) {
             int it = 0;
             bool ok = true;
-            for (int t = pair; t < num_tiles && ok; t += npairs) {
+            for (int t = pair; t < num_units && ok; t += npairs) {
                 int m0, n0;
-                tile_origin(t, m0, n0);
-                // both CTAs' B halves lie in the chunk of n0 (chunks are 256-row multiples)
+                unit_origin(t, m0, n0);
+                const bool half = unit_half(t);
+                // both CTAs' B rows lie in the chunk of n0 (chunks are 256-row multiples)
                 if (gate.flags && !flag_wait_bounded(gate.flags + n0 / gate.rows, gate.epoch,
                                                      &g_status, kErrTcGate)) {
                     ok = false;
@@ -520,11 +544,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
                         break;
                     }
                     // The leader's full barrier counts both CTAs' bytes.
-                    if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
+                    if (leader)
+                        mbar_arrive_expect_tx(&full[s], 2 * (half ? Cfg::A_BYTES + Cfg::B_BYTES / 2
+                                                                  : Cfg::STAGE_BYTES));
                     const uint32_t bar = mapa_shared(&full[s], 0);
                     uint8_t* st = smem + s * Cfg::STAGE_BYTES;
                     tma_load_2d_pair(st, &maps.a, kb * 32, m0 + 128 * rank, bar);
-                    tma_load_2d_pair(st + Cfg::A_BYTES, &maps.b, kb * 32, n0 + 128 * rank, bar);
+                    if (half)
+                        tma_load_2d_pair(st + Cfg::A_BYTES, &maps.b_half, kb * 32, n0 + 64 * rank,
+                                         bar);
+                    else
+                        tma_load_2d_pair(st + Cfg::A_BYTES, &maps.b, kb * 32, n0 + 128 * rank,
+                                         bar);
                 }
             }
             // No copy of this CTA may still be landing when it exits: wait until
@@ -538,7 +569,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         if (leader && lane == 0) {
             bool ok = true;
             int it = 0, cj = 0;
-            for (int t = pair; t < num_tiles && ok; t += npairs) {
+            for (int t = pair; t < num_units && ok; t += npairs) {
+                const bool half = unit_half(t);
                 for (int j = 0; j < nchunks && ok; ++j, ++cj) {
                     const int buf = cj & 1;
                     const uint32_t d_tmem = tmem_base + buf * PBN;
@@ -559,7 +591,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
                         }
                         tc_fence_after();
                         issue_stage_pair<S>(d_tmem, smem_u32(smem + s * Cfg::STAGE_BYTES),
-                                            kb == kb0);
+                                            kb == kb0, half);
                         mma_commit_pair(&empty[s], 0x3);  // frees stage s in both CTAs
                     }
                     if (ok) mma_commit_pair(&acc_full[buf], 0x3);
@@ -579,9 +611,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         const uint32_t leader_empty1 = mapa_shared(&acc_empty[1], 0);
         bool ok = true;
         int cj = 0;
-        for (int t = pair; t < num_tiles && ok; t += npairs) {
+        for (int t = pair; t < num_units && ok; t += npairs) {
             int m0, n0;
-            tile_origin(t, m0, n0);
+            unit_origin(t, m0, n0);
+            // a half-width unit has 128 columns: the second column half's warps
+            // keep in step with the barriers but load and store nothing
+            const bool cols = !unit_half(t) || half == 0;
             const int row = m0 + 128 * static_cast<int>(rank) + q * 32 + lane;
             float acc[128];
 #pragma unroll
@@ -597,18 +632,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
                     break;
                 }
                 tc_fence_after();
+                if (cols) {
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(lane_base + buf * PBN + cc * 32, r);
+                    for (int cc = 0; cc < 4; ++cc) {
+                        uint32_t r[32];
+                        tmem_ld_32x32b_x32(lane_base + buf * PBN + cc * 32, r);
 #pragma unroll
-                    for (int u = 0; u < 32; ++u) acc[cc * 32 + u] += __uint_as_float(r[u]);
+                        for (int u = 0; u < 32; ++u) acc[cc * 32 + u] += __uint_as_float(r[u]);
+                    }
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cluster(buf ? leader_empty1 : leader_empty0);
             }
-            if (ok && row < M) {
+            if (ok && cols && row < M) {
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc) {
                     const int col0 = n0 + half * 128 + cc * 32;
@@ -990,6 +1027,15 @@ int launch_tc(const TcMaps& maps, int M, int N, int K, float alpha, float* C, in
     return cuda_status(cudaGetLastError(), "sgemm_tc");
 }
 
+// ZENGPU_GEMM_TAIL_SPLIT=0 keeps whole tiles in the last wave (same bits either way).
+bool tail_split_enabled() {
+    static const bool enabled = [] {
+        const char* e = std::getenv("ZENGPU_GEMM_TAIL_SPLIT");
+        return !(e && e[0] == '0');
+    }();
+    return enabled;
+}
+
 template <int S>
 int launch_tc_pair(const TcMaps& maps, int M, int N, int K, float alpha, float* C, int64_t ldc,
                    const float* bias, int relu, cudaStream_t s, const GemmGate& gate) {
@@ -1002,8 +1048,15 @@ int launch_tc_pair(const TcMaps& maps, int M, int N, int K, float alpha, float* 
     const int vec_c = (ldc % 4 == 0) && aligned16(C);
     // Persistent grid: one CTA pair per two SMs.
     const int pairs = std::min(tiles, std::max(sm_count() / 2, 1));
+    // Tail split: when the last wave would keep at most half of the pairs busy,
+    // its tiles run as 256 x 128 halves, one per pair, so that wave takes half
+    // as long (4096^3: 3 waves of 74 tiles, then 34 tiles as 68 halves).  The
+    // column width does not change any element's arithmetic.
+    const int rem = tiles % pairs;
+    const bool split = tail_split_enabled() && rem > 0 && 2 * rem <= pairs;
+    const int full_units = split ? tiles - rem : tiles;
     sgemm_tc_pair_kernel<S><<<2 * pairs, kTcThreads, Cfg::SMEM_BYTES, s>>>(
-        maps, M, N, K, alpha, C, ldc, bias, relu, vec_c, gate);
+        maps, M, N, K, alpha, C, ldc, bias, relu, vec_c, gate, full_units, split ? 2 : 1);
     return cuda_status(cudaGetLastError(), "sgemm_tc_pair");
 }
 
@@ -1036,9 +1089,11 @@ int run_tc(const GemmOperands& op, int M, int N, int K, float alpha, float* C, i
     // TF32's A may be the caller's operand: its map covers exactly K columns
     const uint64_t acols = S == 1 ? static_cast<uint64_t>(K) : cols;
     const bool pairs = use_pairs(M, N);
-    // Boxes: 128 rows of A per CTA; B^T 256 rows (one CTA) or 128 (each CTA of a pair).
+    // Boxes: 128 rows of A per CTA; B^T 256 rows (one CTA) or 128 (each CTA of a
+    // pair; 64 for the half-width tail units).
     int rc = encode_map(&maps.a, op.a.p, acols, M, op.a.ld, BM);
     if (!rc) rc = encode_map(&maps.b, op.b.p, cols, N, op.b.ld, pairs ? 128 : BN);
+    if (!rc && pairs) rc = encode_map(&maps.b_half, op.b.p, cols, N, op.b.ld, 64);
     if (rc) return rc;
     if (pairs) return launch_tc_pair<S>(maps, M, N, K, alpha, C, ldc, bias, relu, s, g);
     return launch_tc<S>(maps, M, N, K, alpha, C, ldc, bias, relu, s, g);

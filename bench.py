@@ -57,13 +57,14 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
 # dominant kernel, from one ncu capture of the same workload on a B200:
-#   --metrics dram__bytes_read.sum,dram__bytes_write.sum -k regex:sgemm_tc_pair -s 3 -c 1
-#   on `bench.py --steps 10 --warmup 3 --no-extras` (BF16X3, grouped raster of 8 row-tiles);
+#   BF16X3: --set full -k regex:sgemm_tc_pair -s 3 -c 1 on
+#   `bench.py --steps 4 --warmup 3 --no-extras` (the current kernel; captures of
+#   the same command on other boxes read 2.3-3.8 GB);
 #   the other GEMM modes were captured with the earlier raster of 16 row-tiles;
 #   --section MemoryWorkloadAnalysis -k regex:stream_vec_kernel on the elementwise workload
 # Keyed by the kernel and the per-rank GEMM size (M = N = K) or element count.
 NCU_TRAFFIC = {
-    ("sgemm_tc_pair_kernel<4>", 8192): 3.681e9,
+    ("sgemm_tc_pair_kernel<4>", 8192): 2.687e9,
     ("sgemm_tc_pair_kernel<3>", 8192): 5.642e9,
     ("sgemm_tc_pair_kernel<2>", 8192): 5.999e9,
     ("sgemm_tc_pair_kernel<1>", 8192): 3.105e9,

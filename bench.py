@@ -1099,7 +1099,10 @@ def mlp_measure(torch, K, mode, steps: int, warmup: int) -> dict:
     """op_graph_lower MLP: 4 x (Y = ReLU(X @ W + b)), batch 4096, hidden 4096
     (X normal(0,1) seed 3, W Kaiming-uniform seeds 100.., b uniform[-0.1, 0.1)
     seeds 200..); the fused epilogue vs the unfused gemm -> add(broadcast bias)
-    -> relu chain, each timed over `steps` passes with CUDA events."""
+    -> relu chain, each timed over `steps` passes with CUDA events.  Also the
+    fused chain with the weights packed once beforehand (packed-operand API:
+    each layer packs only its activations), as a caller that reuses weights
+    across passes would run it; it must give the fused chain's bits."""
     bsz = hid = 4096
     layers = 4
     x = torch.empty((bsz, hid), device="cuda")
@@ -1132,9 +1135,27 @@ def mlp_measure(torch, K, mode, steps: int, warmup: int) -> dict:
             h = o
         return h
 
+    packed_w = [K.pack_b(w, mode) for w in ws]  # once, outside the timed region
+    packed_x = [None]
+
+    def fused_packed_weights():
+        h = x
+        for i in range(layers):
+            o = acts[i % 2]
+            pa = K.pack_a(h, mode, out=packed_x[0])
+            packed_x[0] = pa.buf
+            K.sgemm_packed(pa, packed_w[i], o, bias=bs[i], relu=True)
+            h = o
+        return h
+
+    ref = fused().clone()
+    same = bool(torch.equal(fused_packed_weights().view(torch.int32), ref.view(torch.int32)))
+    del ref
+
     res = {}
     clock_summary = None
-    for name, fn in (("fused", fused), ("unfused", unfused)):
+    for name, fn in (("fused", fused), ("unfused", unfused),
+                     ("fused_packed_weights", fused_packed_weights)):
         for _ in range(warmup):
             fn()
         e0, e1 = _event_pair(torch)
@@ -1149,15 +1170,18 @@ def mlp_measure(torch, K, mode, steps: int, warmup: int) -> dict:
         if name == "fused":
             clock_summary = clocks.summary()
     flops = layers * 2.0 * bsz * hid * hid
-    del x, ws, bs, bfull, acts, tmp
+    del x, ws, bs, bfull, acts, tmp, packed_w, packed_x
     torch.cuda.empty_cache()
     return {"fused_ms": res["fused"], "unfused_ms": res["unfused"],
             "tflops_fused": flops / (res["fused"] * 1e-3) / 1e12,
             "tflops_unfused": flops / (res["unfused"] * 1e-3) / 1e12,
             "speedup_fused_vs_unfused": res["unfused"] / res["fused"], "steps": steps,
+            "fused_packed_weights_ms": res["fused_packed_weights"],
+            "tflops_fused_packed_weights": flops / (res["fused_packed_weights"] * 1e-3) / 1e12,
+            "packed_weights_bit_equal_to_fused": same,
             # per layer: the split modes pack A, pack B, kernel; TF32 transposes B then
-            # runs the kernel; SIMT one kernel; unfused adds add + relu
-            "launches_fused": steps * layers * {1: 3, 2: 2, 3: 3, 4: 3}.get(int(mode), 1),
+            # runs the kernel; SIMT transposes A then runs the kernel; unfused adds add + relu
+            "launches_fused": steps * layers * {0: 2, 1: 3, 2: 2, 3: 3, 4: 3}.get(int(mode), 1),
             "clocks": clock_summary,
             "workload": "op_graph_lower MLP 4 x relu(X@W+b), X 4096x4096, W 4096x4096"}
 
@@ -1239,6 +1263,11 @@ def mlp_workload(args, torch, zg, K, mode, peaks, peak_src, world):
                    "speedup_fused_vs_unfused": r["speedup_fused_vs_unfused"]},
         "gpu_launches": r["launches_fused"],
         "clocks": r["clocks"],
+        "packed_weights": {"ms_per_step": r["fused_packed_weights_ms"],
+                           "tflops": r["tflops_fused_packed_weights"],
+                           "bit_equal_to_fused": r["packed_weights_bit_equal_to_fused"],
+                           "what": "weights packed once beforehand (packed-operand API); "
+                                   "each layer packs its activations and runs the kernel"},
     }
 
 

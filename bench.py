@@ -1153,7 +1153,7 @@ def mlp_measure(torch, K, mode, steps: int, warmup: int) -> dict:
     del ref
 
     res = {}
-    clock_summary = None
+    clock_summary = packed_clocks = None
     for name, fn in (("fused", fused), ("unfused", unfused),
                      ("fused_packed_weights", fused_packed_weights)):
         for _ in range(warmup):
@@ -1169,6 +1169,8 @@ def mlp_measure(torch, K, mode, steps: int, warmup: int) -> dict:
         res[name] = e0.elapsed_time(e1) / steps
         if name == "fused":
             clock_summary = clocks.summary()
+        if name == "fused_packed_weights":
+            packed_clocks = clocks.summary()
     flops = layers * 2.0 * bsz * hid * hid
     del x, ws, bs, bfull, acts, tmp, packed_w, packed_x
     torch.cuda.empty_cache()
@@ -1179,6 +1181,7 @@ def mlp_measure(torch, K, mode, steps: int, warmup: int) -> dict:
             "fused_packed_weights_ms": res["fused_packed_weights"],
             "tflops_fused_packed_weights": flops / (res["fused_packed_weights"] * 1e-3) / 1e12,
             "packed_weights_bit_equal_to_fused": same,
+            "packed_weights_clocks": packed_clocks,
             # per layer: the split modes pack A, pack B, kernel; TF32 transposes B then
             # runs the kernel; SIMT transposes A then runs the kernel; unfused adds add + relu
             "launches_fused": steps * layers * {0: 2, 1: 3, 2: 2, 3: 3, 4: 3}.get(int(mode), 1),
@@ -1266,6 +1269,7 @@ def mlp_workload(args, torch, zg, K, mode, peaks, peak_src, world):
         "packed_weights": {"ms_per_step": r["fused_packed_weights_ms"],
                            "tflops": r["tflops_fused_packed_weights"],
                            "bit_equal_to_fused": r["packed_weights_bit_equal_to_fused"],
+                           "clocks": r["packed_weights_clocks"],
                            "what": "weights packed once beforehand (packed-operand API); "
                                    "each layer packs its activations and runs the kernel"},
     }

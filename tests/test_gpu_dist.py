@@ -90,8 +90,15 @@ def _run(world, **kw):
 
 @pytest.mark.parametrize("mode", [3, 1, 2, 4], ids=["TF32_BF16X2", "TF32X3", "TF32", "BF16X3"])
 def test_chained_gemm_two_ranks(mode):
-    # 2 x 1024 rows: 128 x 256 tiles (single-CTA kernel); chunks of 256 columns
+    # 2 x 1024 rows: 64 tiles of 256 x 256 per rank (CTA-pair kernel); chunks of 256 columns
     _run(2, mode=mode, m_total=2048, n=4096, k=1024, chunk=256)
+
+
+@pytest.mark.parametrize("mode", [4, 1], ids=["BF16X3", "TF32X3"])
+def test_chained_gemm_single_cta_kernel(mode):
+    # 2 x 256 rows, 1024 columns: 4 tiles of 256 x 256 per rank, below the pair
+    # kernel's 8, so the gated GEMM runs one CTA per 128 x 256 tile
+    _run(2, mode=mode, m_total=512, n=1024, k=768, chunk=256)
 
 
 def test_chained_gemm_pair_kernel_ragged():
@@ -101,6 +108,7 @@ def test_chained_gemm_pair_kernel_ragged():
 
 
 def test_chained_gemm_source_not_rank0():
+    # 2 x 512 rows: 16 tiles per rank, run as 32 half-width (256 x 128) units
     _run(2, mode=3, m_total=1024, n=2048, k=512, chunk=256, src=1)
 
 
